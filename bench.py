@@ -1,0 +1,412 @@
+"""Benchmark of the B200 AWA layer (SeedVR2 adaptive window attention).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload cfg4]
+
+Metric: AWA attention windows/s (and TFLOPS) per B200, against
+the reference's ncnn CPU path. A step is one AWA layer forward -- Pack ->
+MMRoPE -> WindowAttention -> Unpack, run as the fused chain awa_forward --
+over one synthetic batch of the workload's shape, inputs resident in HBM.
+
+* value      windows of all ranks / max-over-ranks device time (CUDA events)
+* e2e        same metric through the C ABI with host buffers: pinned-host ->
+             device copy of the step's QKV, the forward, device -> host copy of
+             the outputs, every step inside the timed region
+* roofline   the dominant kernel (fused tcgen05 attention), timed live by the
+             library's launch profiler (events on its own stream)
+* cpu_baseline  the reference's own awa_layers.cpp CPU forward (oracle/_ref),
+             on a bounded sample of cfg4-shaped windows, scaled by sum(L^2)
+
+N > 1 (torchrun, one rank per GPU): every rank runs its own layer instance (an
+independent clip / CFG branch): weak scaling, no collective on the data path.
+--impl reference times the reference CPU path on all host cores (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import multiprocessing as mp
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "seedvr2-ncnn_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "AWA attention TFLOPS & windows/s per B200 (1/2/4/8 GPU) vs ncnn CPU ref"
+UNIT = "windows/s"
+HEADS, HEAD_DIM, TEXT = 20, 128, 58
+
+WORKLOADS = {
+    # name: (grid, num_windows, shifted, precision, description)
+    "cfg4": ((21, 64, 64), (6, 8, 8), 0, "bf16",
+             "81x1024x1024 video -> 21x64x64 latent grid, 4x8x8 windows (num_windows 6,8,8), unshifted"),
+    "cfg4-shifted": ((21, 64, 64), (6, 8, 8), 1, "bf16",
+                     "21x64x64 grid, 4x8x8 windows shifted by (2,4,4), partial edge windows"),
+    "cfg5": ((9, 45, 80), (3, 6, 10), 0, "bf16", "33x720x1280 video -> 9x45x80 grid, adaptive 3x8x8 windows"),
+    "cfg5-fp32": ((9, 45, 80), (3, 6, 10), 0, "fp32", "9x45x80 grid, adaptive 3x8x8 windows, fp32 block"),
+    "cfg2": ((6, 16, 16), (2, 8, 8), 0, "bf16", "21x256x256 video -> 6x16x16 grid, 3x8x8 windows"),
+}
+
+
+def window_costs(grid, num, shifted):
+    import awa_b200
+
+    wins = awa_b200.make_windows(grid, num, bool(shifted))
+    lengths = [(w[1] - w[0]) * (w[3] - w[2]) * (w[5] - w[4]) + TEXT for w in wins]
+    return wins, lengths
+
+
+def attention_flops(lengths, heads=HEADS, head_dim=HEAD_DIM):
+    return float(sum(4.0 * L * L * head_dim * heads for L in lengths))
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def _ref_sample_worker(args):
+    """Runs the reference's CPU chain on one sample; returns (seconds, sum L^2 * heads)."""
+    grid, num, heads, seed = args
+    import numpy as np
+
+    from oracle.oracle import LayerConfig, Reference
+
+    ref = Reference()
+    cfg = LayerConfig(*grid, *num, text_tokens=TEXT, shifted=0, heads=heads, head_dim=HEAD_DIM)
+    rng = np.random.default_rng(seed)
+    v = rng.standard_normal((cfg.source_tokens, 3, heads, HEAD_DIM), dtype=np.float32)
+    t = rng.standard_normal((TEXT, 3, heads, HEAD_DIM), dtype=np.float32)
+    start = time.perf_counter()
+    ref.chain(cfg, v, t)
+    seconds = time.perf_counter() - start
+    wins = ref.make_windows(grid, num, False)
+    work = sum(((w[1] - w[0]) * (w[3] - w[2]) * (w[5] - w[4]) + TEXT) ** 2 for w in wins) * heads
+    return seconds, work
+
+
+def cpu_kind():
+    from oracle.oracle import Reference
+
+    return "reference" if Reference.available() else "port"
+
+
+def cpu_baseline_single(workload_work, workload_windows, budget_s=12.0):
+    """Reference CPU forward, 1 core, on 4 windows of the cfg4 window shape
+    (grid 4x16x16, num_windows 1,8,8: four 4x8x8 windows + 58 text tokens,
+    20 heads), repeated for ~budget_s; scaled to the workload by sum(L^2)."""
+    sample = ((4, 16, 16), (1, 8, 8), HEADS)
+    total_s, total_work, reps = 0.0, 0.0, 0
+    while total_s < budget_s and reps < 8:
+        s, w = _ref_sample_worker((*sample, reps))
+        total_s += s
+        total_work += w
+        reps += 1
+    layer_seconds = total_s * (workload_work / total_work)
+    return {
+        "value": workload_windows / layer_seconds,
+        "unit": UNIT,
+        "cores": 1,
+        "kind": cpu_kind(),
+        "sample": f"{reps} runs of the reference Pack->MMRoPE->WindowAttention->Unpack CPU forward on a "
+                  f"4x16x16 grid with num_windows (1,8,8): 4 windows of 4x8x8 video + {TEXT} text tokens, "
+                  f"{HEADS} heads x {HEAD_DIM} (cfg4's window shape), {total_s:.1f} s; scaled to the workload "
+                  f"by sum(L^2)*heads",
+        "seconds": round(total_s, 3),
+    }
+
+
+def run_reference_arm(args, rank, world):
+    """--impl reference: the reference CPU path on every host core (rank 0 only)."""
+    if rank != 0:
+        return None
+    name = args.workload
+    grid, num, shifted, precision, desc = WORKLOADS[name]
+    _, lengths = window_costs(grid, num, shifted)
+    workload_work = sum(L * L for L in lengths) * HEADS
+    cores = os.cpu_count() or 1
+    # One cfg4-shaped window per worker per step; heads trimmed so the whole
+    # run stays within ~4 minutes.
+    per_window_s = 0.55
+    heads = HEADS
+    budget = 240.0
+    if (args.steps + args.warmup) * per_window_s > budget:
+        heads = max(1, int(HEADS * budget / ((args.steps + args.warmup) * per_window_s)))
+    sample = ((4, 8, 8), (1, 8, 8), heads)
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(cores) as pool:
+        for i in range(args.warmup):
+            pool.map(_ref_sample_worker, [(*sample, i * cores + c) for c in range(cores)])
+        start = time.perf_counter()
+        work = 0.0
+        for i in range(args.steps):
+            res = pool.map(_ref_sample_worker, [(*sample, 10_000 + i * cores + c) for c in range(cores)])
+            work += sum(w for _, w in res)
+        elapsed = time.perf_counter() - start
+    layer_seconds = elapsed * workload_work / work
+    value = len(lengths) / layer_seconds
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed * 1000 / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
+        "config": {"workload": name, "description": desc, "heads": HEADS, "head_dim": HEAD_DIM, "text_tokens": TEXT},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": cpu_kind(),
+                         "sample": f"per step, {cores} processes each run the reference CPU chain on one "
+                                   f"cfg4-shaped window (4x8x8 video + {TEXT} text, {heads} heads); "
+                                   f"scaled to the workload by sum(L^2)*heads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    return line
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(device_index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
+        sm, sm_max, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                sm_max = float(r[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        loaded = [s for s in sm if sm_max and s > 0.5 * sm_max] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": sm_max,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- B200 arm
+def run_b200(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import awa_b200
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    name = args.workload
+    grid, num, shifted, precision, desc = WORKLOADS[name]
+    prec = awa_b200.AWA_PREC_BF16 if precision == "bf16" else awa_b200.AWA_PREC_FP32
+    dtype = torch.bfloat16 if precision == "bf16" else torch.float32
+    esize = 2 if precision == "bf16" else 4
+    wins, lengths = window_costs(grid, num, shifted)
+    W = len(lengths)
+    flops = attention_flops(lengths)
+    n_v = grid[0] * grid[1] * grid[2]
+    plan = awa_b200.AwaPlan(*grid, *num, text_tokens=TEXT, shifted=bool(shifted))
+    kernel_kind = plan.attention_kernel_kind(prec, HEADS, HEAD_DIM)
+
+    gen = torch.Generator(device=device).manual_seed(1234 + rank)
+    video_qkv = torch.randn(n_v, 3, HEADS, HEAD_DIM, device=device, generator=gen).to(dtype)
+    text_qkv = torch.randn(TEXT, 3, HEADS, HEAD_DIM, device=device, generator=gen).to(dtype)
+    video_out = torch.empty(n_v, HEADS, HEAD_DIM, device=device, dtype=dtype)
+    text_out = torch.empty(TEXT, HEADS, HEAD_DIM, device=device, dtype=dtype)
+    workspace = torch.empty(plan.workspace_bytes(HEADS, HEAD_DIM), device=device, dtype=torch.uint8)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        plan.forward(video_qkv, text_qkv, prec, out_dtype=dtype, workspace=workspace, video_out=video_out,
+                     text_out=text_out, stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    clocks = ClockSampler(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                          int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank]))
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    awa_b200.device_status()
+
+    # ---- device-resident timed region (inputs 1.3 GB >> 126 MB L2: no flush needed)
+    awa_b200.profile_reset()
+    awa_b200.profile_enable(True)
+    barrier()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    stop.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    awa_b200.profile_enable(False)
+    prof = awa_b200.profile_collect()
+    elapsed_ms = start.elapsed_time(stop)
+    t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    ms_per_step = max_ms / args.steps
+    value = W * world / (ms_per_step / 1000.0)
+    launches = sum(v[0] for v in prof.values())
+
+    # ---- end to end through the C ABI with host buffers
+    e2e_steps = max(3, min(args.steps, args.e2e_steps))
+    host_v = torch.empty(video_qkv.shape, dtype=dtype, pin_memory=True)
+    host_t = torch.empty(text_qkv.shape, dtype=dtype, pin_memory=True)
+    host_v.copy_(video_qkv)
+    host_t.copy_(text_qkv)
+    out_v = torch.empty(video_out.shape, dtype=dtype, pin_memory=True)
+    out_t = torch.empty(text_out.shape, dtype=dtype, pin_memory=True)
+    dev_v = torch.empty_like(video_qkv)
+    dev_t = torch.empty_like(text_qkv)
+
+    def e2e_step():
+        dev_v.copy_(host_v, non_blocking=True)
+        dev_t.copy_(host_t, non_blocking=True)
+        plan.forward(dev_v, dev_t, prec, out_dtype=dtype, workspace=workspace, video_out=video_out,
+                     text_out=text_out, stream=stream)
+        out_v.copy_(video_out, non_blocking=True)
+        out_t.copy_(text_out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e_stop.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    te = torch.tensor([e_start.elapsed_time(e_stop)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item()) / e2e_steps
+    clock = clocks.stop()
+    awa_b200.device_status()
+
+    # ---- roofline of the dominant kernel
+    attn_name = next((k for k in prof if k.startswith("awa_attention")), None)
+    attn_launches, attn_ms_total = prof.get(attn_name, (0, 0.0))
+    attn_ms = attn_ms_total / max(attn_launches, 1)
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    hbm_peak = peaks.get("hbm_gbs")
+    tensor_peak = peaks.get("bf16_tflops")
+    peak_src = "measured" if hbm_peak else "fallback"
+    hbm_peak = hbm_peak or 6650.0
+    tensor_peak = tensor_peak or 1590.0
+    in_bytes = (n_v + TEXT) * 3 * HEADS * HEAD_DIM * esize
+    out_bytes = (n_v + TEXT) * HEADS * HEAD_DIM * esize
+    alg_bytes = in_bytes + out_bytes  # read the source QKV once, write the outputs once
+    achieved_gbs = alg_bytes / (attn_ms / 1000.0) / 1e9
+    achieved_tflops = flops / (attn_ms / 1000.0) / 1e12
+    traffic = None
+    traffic_file = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(traffic_file) as f:
+            traffic = json.load(f).get(f"{name}:{attn_name}")
+    except (OSError, ValueError):
+        traffic = None
+    roofline = {
+        "bound": "hbm", "kernel": attn_name, "achieved": round(achieved_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+        "frac": round(achieved_gbs / hbm_peak, 4), "traffic": traffic, "peak_source": peak_src,
+        "algorithmic_bytes": alg_bytes, "kernel_ms": round(attn_ms, 5),
+        "tensor": {"achieved_tflops": round(achieved_tflops, 1), "peak_tflops": tensor_peak,
+                   "frac": round(achieved_tflops / tensor_peak, 4), "flops": flops},
+    }
+
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": precision, "data": "synthetic N(0,1) QKV, seeded",
+            "config": {"workload": name, "description": desc, "grid": list(grid), "num_windows": list(num),
+                       "shifted": bool(shifted), "windows": W, "heads": HEADS, "head_dim": HEAD_DIM,
+                       "text_tokens": TEXT, "rope_dim": 126, "precision": precision,
+                       "attention_kernel": "tcgen05" if kernel_kind == 1 else "simt",
+                       "l2": f"inputs {in_bytes / 1e9:.2f} GB per step > 126 MB L2; no flush",
+                       "parallelism": f"weak: {world} independent layer(s), one per GPU"},
+            "attn_tflops": round(flops * world / (ms_per_step / 1000.0) / 1e12, 2),
+            "gpu_launches": launches,
+            "e2e": {"value": round(W * world / (e2e_ms / 1000.0), 2), "unit": UNIT,
+                    "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes, "steps": e2e_steps,
+                    "ms_per_step": round(e2e_ms, 4)},
+            "roofline": roofline,
+            "clocks": clock,
+            "profile": {k: {"launches": v[0], "ms": round(v[1], 4)} for k, v in prof.items()},
+        }
+    return line
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=200)
+    parser.add_argument("--warmup", type=int, default=10)
+    parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    parser.add_argument("--workload", default="cfg4", choices=sorted(WORKLOADS))
+    parser.add_argument("--e2e-steps", type=int, default=20)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("--warmup must be >= 3")
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        line = run_reference_arm(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_b200(args, rank, world, local_rank)
+        if rank == 0:
+            if world == 1 and not args.no_cpu_baseline:
+                grid, num, shifted, _, _ = WORKLOADS[args.workload]
+                _, lengths = window_costs(grid, num, shifted)
+                line["cpu_baseline"] = cpu_baseline_single(sum(L * L for L in lengths) * HEADS, len(lengths))
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,215 @@
+/*
+ * awa_b200.h -- C ABI of the B200 (sm_100a) adaptive window attention (AWA)
+ * layers of SeedVR2. Drop-in for the four ncnn custom layers of
+ * HGinkgo/SeedVR2-ncnn src/awa (SeedVR2AWAPack -> SeedVR2MMRoPE ->
+ * SeedVR2WindowAttention -> SeedVR2AWAUnpack); the ncnn-compatible C++ layer
+ * classes in seedvr2-ncnn_b200/ncnn_compat/ call these entry points.
+ *
+ * Conventions (same as the ncnn layers they replace):
+ *   - status codes: 0 ok, -1 invalid shape / params / state, -100 allocation
+ *     failure (awa_layers.cpp:411, 424, 439, 509); this library adds -2 for a
+ *     CUDA runtime error and -3 for a device-side check that failed. The text
+ *     of the last error of the calling thread is in awa_last_error().
+ *   - every tensor argument is a DEVICE pointer on the plan's device, except
+ *     where a function says "host"; strides are in elements, not bytes.
+ *   - all work is enqueued on the given stream; nothing synchronises.
+ *   - inputs are const; outputs are written completely (no accumulation).
+ *   - the QKV blob of a layer is addressed as
+ *       base + token * token_stride + qkv * qkv_stride + head * head_dim + f
+ *     which covers every encoding describe_qkv_layout accepts
+ *     (awa_layers.cpp:116-175): (w=d,h=3H,c=N) -> token_stride=cstep,
+ *     qkv_stride=H*d; (w=d,h=H,c=3N) -> token_stride=cstep, qkv_stride=N*cstep;
+ *     (w=d,h=H,d=3,c=N) -> token_stride=cstep, qkv_stride=H*d.
+ *   - packed / attended / output blobs are one row of [rows][head_dim] per
+ *     token with a token stride (ncnn cstep): packed QKV rows hold 3*H rows
+ *     (q heads, k heads, v heads), attended / output rows hold H rows.
+ */
+#ifndef AWA_B200_H
+#define AWA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* awa_stream_t; /* identical to cudaStream_t */
+typedef struct awa_plan awa_plan;
+
+#define AWA_OK 0
+#define AWA_ERR_INVALID (-1)
+#define AWA_ERR_CUDA (-2)
+#define AWA_ERR_DEVICE (-3)
+#define AWA_ERR_ALLOC (-100)
+
+/* element types of blobs */
+#define AWA_F32 0
+#define AWA_BF16 1
+
+/* attention arithmetic */
+#define AWA_PREC_FP32 0 /* fp32 FFMA, fp32 accumulation, no TF32 (fp32 blocks) */
+#define AWA_PREC_BF16 1 /* bf16 operands on tcgen05 tensor cores, fp32 accumulation (bf16 blocks) */
+
+/* ParamDict ids 0-8 of the AWA layers (awa_layers.cpp:90-114, 872).
+ * source_t/h/w == -1,-1,-1 means "take the grid from the runtime spec". */
+typedef struct
+{
+    int source_t, source_h, source_w; /* ids 0,1,2: latent grid T x H x W */
+    int windows_t, windows_h, windows_w; /* ids 3,4,5: target window COUNTS */
+    int text_tokens;                  /* id 6 */
+    int shifted;                      /* id 7: half-window shift (odd blocks) */
+    int rope_dim;                     /* id 8: rotated features of Q/K, multiple of 6 (reference default 126) */
+} awa_layer_params;
+
+/* seedvr2::AwaRuntimeSpec (awa_layers.h:31-39). */
+typedef struct
+{
+    int source_t, source_h, source_w, video_tokens;
+} awa_runtime_spec;
+
+/* seedvr2::AwaWindow (awa_layers.h:20-28): [t0,t1) x [h0,h1) x [w0,w1). */
+typedef struct
+{
+    int t0, t1, h0, h1, w0, w1;
+} awa_window;
+
+typedef struct
+{
+    int source_t, source_h, source_w;
+    int source_tokens;   /* N_v */
+    int text_tokens;
+    int window_count;    /* W */
+    int sequence_tokens; /* S = sum of window lengths (video tokens + text tokens) */
+    int max_window_length;
+    int rope_dim;
+    int shifted;
+    int device;          /* CUDA device the plan's tables live on */
+} awa_plan_info;
+
+/* Replaces seedvr2::make_awa_windows (awa_layers.cpp:347-359, window rule
+ * :53-88). Host only. Writes min(count, capacity) windows; returns the window
+ * count, 0 for non-positive arguments. */
+int awa_make_windows(int source_t, int source_h, int source_w, int windows_t, int windows_h, int windows_w,
+                     int shifted, awa_window* out, int capacity);
+
+/* Replaces the load_param of all four layers (awa_layers.cpp:382-417,
+ * 599-636, 867-911, 1046-1060): builds the windows, index maps, cu_seqlens and
+ * the RoPE table on the host and uploads them once to the CURRENT device.
+ * spec may be NULL; it is required when params->source_* are -1 and must then
+ * satisfy AwaRuntimeSpec::valid (awa_layers.cpp:340-345). rope_dim <= 0 means
+ * 126. Returns -1 for what load_param rejects, -100 if an allocation fails. */
+int awa_plan_create(const awa_layer_params* params, const awa_runtime_spec* spec, awa_plan** out_plan);
+/* Same as awa_plan_create but builds the host tables only (no device, no
+ * upload): for inspecting index maps on machines without a GPU. Every forward
+ * entry point rejects such a plan with -1. */
+int awa_plan_create_host(const awa_layer_params* params, const awa_runtime_spec* spec, awa_plan** out_plan);
+void awa_plan_destroy(awa_plan* plan);
+int awa_plan_get_info(const awa_plan* plan, awa_plan_info* info);
+
+/* Host copies of the plan's index maps, for bit-exact checks. Each pointer may
+ * be NULL; sizes are S, W+1, N_v and W*text_tokens ints. Windows: W entries. */
+int awa_plan_get_maps(const awa_plan* plan, int* sequence_index, int* cu_seqlens, int* video_positions,
+                      int* text_positions, awa_window* windows);
+
+/* Replaces SeedVR2AWAPack::forward (awa_layers.cpp:419-458 CPU, 501-578 Vulkan).
+ * packed: S rows of 3*H*head_dim (stride packed_token_stride >= 3*H*head_dim);
+ * cu_seqlens: W+1 floats (the reference stores them as float). */
+int awa_pack(const awa_plan* plan, int heads, int head_dim, int in_dtype, const void* video_qkv,
+             int64_t video_token_stride, int64_t video_qkv_stride, const void* text_qkv, int64_t text_token_stride,
+             int64_t text_qkv_stride, int out_dtype, void* packed, int64_t packed_token_stride, float* cu_seqlens,
+             awa_stream_t stream);
+
+/* Replaces SeedVR2MMRoPE::forward (awa_layers.cpp:913-953, 985-1025): rotates
+ * the first rope_dim features of the Q and K rows in interleaved pairs;
+ * V rows and the tail are copied. In fp32 the result is bit-identical to the
+ * reference CPU forward. in and out may not alias. */
+int awa_mmrope(const awa_plan* plan, int heads, int head_dim, int in_dtype, const void* packed_in,
+               int64_t in_token_stride, int out_dtype, void* packed_out, int64_t out_token_stride,
+               awa_stream_t stream);
+
+/* Replaces SeedVR2WindowAttention::forward (awa_layers.cpp:1062-1120,
+ * 1152-1234): per window and head, softmax(Q K^T / sqrt(d)) V over the
+ * window's packed rows, no mask. Output: S rows of H*head_dim. */
+int awa_window_attention(const awa_plan* plan, int precision, int heads, int head_dim, int in_dtype,
+                         const void* packed, int64_t in_token_stride, int out_dtype, void* attended,
+                         int64_t out_token_stride, awa_stream_t stream);
+
+/* Replaces SeedVR2AWAUnpack::forward (awa_layers.cpp:638-689, 743-846):
+ * video rows back to source order, text rows = mean over windows (sum of
+ * x / W in window order, as the CPU forward). */
+int awa_unpack(const awa_plan* plan, int heads, int head_dim, int in_dtype, const void* attended,
+               int64_t in_token_stride, int out_dtype, void* video_out, int64_t video_token_stride,
+               void* text_out, int64_t text_token_stride, awa_stream_t stream);
+
+/* The whole chain Pack -> MMRoPE -> WindowAttention -> Unpack in one pass:
+ * gathers each window's rows from the source QKV, rotates Q/K on the fly,
+ * attends, scatters video rows to source order and reduces the text rows, so
+ * no packed intermediate is written. Needs a workspace of
+ * awa_forward_workspace_bytes(). Outputs equal the four-layer chain's. */
+size_t awa_forward_workspace_bytes(const awa_plan* plan, int heads, int head_dim);
+int awa_forward(const awa_plan* plan, int precision, int heads, int head_dim, int in_dtype, const void* video_qkv,
+                int64_t video_token_stride, int64_t video_qkv_stride, const void* text_qkv,
+                int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype, void* video_out,
+                int64_t video_token_stride_out, void* text_out, int64_t text_token_stride_out, void* workspace,
+                size_t workspace_bytes, awa_stream_t stream);
+
+/* Window-parallel form of awa_forward for one rank of a multi-GPU group:
+ * computes only the windows [window_begin, window_end) of the plan's window
+ * order (every token of those windows is written to video_out; other rows
+ * are left untouched) and writes the UNNORMALISED text partial sum
+ * sum_{w in range} attended_text(w) to text_partial (fp32, text_tokens x H x
+ * head_dim, dense). The caller all-reduces the partials and calls
+ * awa_text_finalize. */
+int awa_forward_windows(const awa_plan* plan, int precision, int heads, int head_dim, int window_begin,
+                        int window_end, int in_dtype, const void* video_qkv, int64_t video_token_stride,
+                        int64_t video_qkv_stride, const void* text_qkv, int64_t text_token_stride,
+                        int64_t text_qkv_stride, int out_dtype, void* video_out, int64_t video_token_stride_out,
+                        float* text_partial, void* workspace, size_t workspace_bytes, awa_stream_t stream);
+
+/* text_out = text_sum / W (all windows of the plan), converted to out_dtype. */
+int awa_text_finalize(const awa_plan* plan, int heads, int head_dim, const float* text_sum, int out_dtype,
+                      void* text_out, int64_t text_token_stride, awa_stream_t stream);
+
+/* Gathered-shard scatter for the multi-GPU path: rows of the packed video
+ * shard layout (windows [window_begin, window_end) in plan order, video rows
+ * only, dense H*head_dim rows) are copied to their source-order rows. */
+int awa_scatter_video_shard(const awa_plan* plan, int heads, int head_dim, int window_begin, int window_end,
+                            int dtype, const void* shard, void* video_out, int64_t video_token_stride,
+                            awa_stream_t stream);
+int awa_gather_video_shard(const awa_plan* plan, int heads, int head_dim, int window_begin, int window_end,
+                           int dtype, const void* video, int64_t video_token_stride, void* shard,
+                           awa_stream_t stream);
+/* Number of video rows of windows [window_begin, window_end). */
+int64_t awa_window_range_video_rows(const awa_plan* plan, int window_begin, int window_end);
+/* Splits the plan's windows into `parts` contiguous ranges of near-equal
+ * attention cost (sum of L^2); bounds receives parts+1 window indices. */
+int awa_partition_windows(const awa_plan* plan, int parts, int* bounds);
+
+/* Device-side status of the library on the current device: 0, or the code of
+ * the first device check that failed since the last call (a bounded wait that
+ * gave up). Synchronises the device. Clears the flag. */
+int awa_device_status(void);
+
+/* Which attention kernel awa_window_attention / awa_forward would launch for
+ * these arguments: 1 = tcgen05 (sm_100a tensor cores), 2 = fp32 SIMT. */
+int awa_attention_kernel_kind(const awa_plan* plan, int precision, int heads, int head_dim);
+
+/* Opt-in launch profiler (the counterpart of the reference's
+ * PerformanceProfile, src/inference/performance_profile.h:75-227): while
+ * enabled, every kernel the library launches is bracketed by CUDA events on
+ * its own stream. awa_profile_collect synchronises those events and returns,
+ * per kernel name, the launch count and total device milliseconds, formatted
+ * as "profile name=<kernel> launches=<n> ms=<total>\n" lines. */
+void awa_profile_enable(int enabled);
+void awa_profile_reset(void);
+int awa_profile_collect(char* buffer, size_t capacity);
+
+const char* awa_last_error(void);
+const char* awa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AWA_B200_H */

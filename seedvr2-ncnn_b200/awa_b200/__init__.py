@@ -1,0 +1,436 @@
+"""Python binding of the B200 AWA library (include/awa_b200.h) over ctypes.
+
+The library is the CUDA implementation of SeedVR2-ncnn's adaptive window
+attention layers (src/awa): ``AwaPlan`` is what the four ncnn layers build in
+``load_param``; its methods are the layers' forwards (``pack``, ``mmrope``,
+``window_attention``, ``unpack``) and the fused chain (``forward``). Tensors
+are torch CUDA tensors; torch is used only for device memory and streams.
+
+There is no CPU fallback: importing this module on a machine without the
+built library raises, and every call needs a CUDA device.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+from typing import List, Optional, Sequence, Tuple
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_DIR, "lib", "libawa_b200.so")
+COMPAT_PATH = os.path.join(PKG_DIR, "lib", "libawa_ncnn_compat.so")
+
+AWA_F32 = 0
+AWA_BF16 = 1
+AWA_PREC_FP32 = 0
+AWA_PREC_BF16 = 1
+AWA_OK = 0
+AWA_ERR_INVALID = -1
+AWA_ERR_CUDA = -2
+AWA_ERR_DEVICE = -3
+AWA_ERR_ALLOC = -100
+
+# Every symbol declared in include/awa_b200.h.
+EXPORTED_SYMBOLS = (
+    "awa_make_windows", "awa_plan_create", "awa_plan_create_host", "awa_plan_destroy", "awa_plan_get_info", "awa_plan_get_maps",
+    "awa_pack", "awa_mmrope", "awa_window_attention", "awa_unpack", "awa_forward_workspace_bytes", "awa_forward",
+    "awa_forward_windows", "awa_text_finalize", "awa_scatter_video_shard", "awa_gather_video_shard",
+    "awa_window_range_video_rows", "awa_partition_windows", "awa_device_status", "awa_attention_kernel_kind",
+    "awa_profile_enable", "awa_profile_reset", "awa_profile_collect", "awa_last_error", "awa_version",
+)
+
+
+class AwaError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"awa error {code}: {message}")
+        self.code = code
+
+
+class _LayerParams(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("source_t", "source_h", "source_w", "windows_t", "windows_h",
+                                             "windows_w", "text_tokens", "shifted", "rope_dim")]
+
+
+class _RuntimeSpec(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("source_t", "source_h", "source_w", "video_tokens")]
+
+
+class _Window(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("t0", "t1", "h0", "h1", "w0", "w1")]
+
+
+class _PlanInfo(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("source_t", "source_h", "source_w", "source_tokens", "text_tokens",
+                                             "window_count", "sequence_tokens", "max_window_length", "rope_dim",
+                                             "shifted", "device")]
+
+
+_lib = None
+
+
+def library() -> ctypes.CDLL:
+    """Load lib/libawa_b200.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.isfile(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with `make -C {PKG_DIR}` (no CPU fallback exists)")
+    lib = ctypes.CDLL(LIB_PATH)
+    i, p, i64, sz = ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_size_t
+    sig = {
+        "awa_make_windows": (i, [i, i, i, i, i, i, i, p, i]),
+        "awa_plan_create": (i, [p, p, ctypes.POINTER(p)]),
+        "awa_plan_create_host": (i, [p, p, ctypes.POINTER(p)]),
+        "awa_plan_destroy": (None, [p]),
+        "awa_plan_get_info": (i, [p, p]),
+        "awa_plan_get_maps": (i, [p, p, p, p, p, p]),
+        "awa_pack": (i, [p, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, p]),
+        "awa_mmrope": (i, [p, i, i, i, p, i64, i, p, i64, p]),
+        "awa_window_attention": (i, [p, i, i, i, i, p, i64, i, p, i64, p]),
+        "awa_unpack": (i, [p, i, i, i, p, i64, i, p, i64, p, i64, p]),
+        "awa_forward_workspace_bytes": (sz, [p, i, i]),
+        "awa_forward": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p, sz, p]),
+        "awa_forward_windows": (i, [p, i, i, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, p, sz, p]),
+        "awa_text_finalize": (i, [p, i, i, p, i, p, i64, p]),
+        "awa_scatter_video_shard": (i, [p, i, i, i, i, i, p, p, i64, p]),
+        "awa_gather_video_shard": (i, [p, i, i, i, i, i, p, i64, p, p]),
+        "awa_window_range_video_rows": (i64, [p, i, i]),
+        "awa_partition_windows": (i, [p, i, p]),
+        "awa_device_status": (i, []),
+        "awa_attention_kernel_kind": (i, [p, i, i, i]),
+        "awa_profile_enable": (None, [i]),
+        "awa_profile_reset": (None, []),
+        "awa_profile_collect": (i, [p, sz]),
+        "awa_last_error": (ctypes.c_char_p, []),
+        "awa_version": (ctypes.c_char_p, []),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def _check(rc: int) -> None:
+    if rc != AWA_OK:
+        raise AwaError(rc, library().awa_last_error().decode())
+
+
+def make_windows(size: Sequence[int], num_windows: Sequence[int], shifted: bool) -> List[Tuple[int, ...]]:
+    """Window bounds (t0, t1, h0, h1, w0, w1) in layer order (host only, no GPU needed)."""
+    lib = library()
+    n = lib.awa_make_windows(*size, *num_windows, int(shifted), None, 0)
+    arr = (_Window * max(n, 1))()
+    lib.awa_make_windows(*size, *num_windows, int(shifted), ctypes.cast(arr, ctypes.c_void_p), n)
+    return [(w.t0, w.t1, w.h0, w.h1, w.w0, w.w1) for w in arr[:n]]
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _dtype_code(t) -> int:
+    torch = _torch()
+    if t.dtype == torch.float32:
+        return AWA_F32
+    if t.dtype == torch.bfloat16:
+        return AWA_BF16
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+def _torch_dtype(code: int):
+    torch = _torch()
+    return torch.float32 if code == AWA_F32 else torch.bfloat16
+
+
+def _stream_ptr(stream) -> Optional[int]:
+    torch = _torch()
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return stream.cuda_stream
+
+
+def _qkv_strides(t) -> Tuple[int, int]:
+    """(token_stride, qkv_stride) of a [tokens, 3, H, d] view with dense (H, d)."""
+    if t.dim() != 4 or t.shape[1] != 3 or t.stride(3) != 1 or t.stride(2) != t.shape[3]:
+        raise ValueError("QKV tensors must be [tokens, 3, heads, head_dim] with dense heads x head_dim")
+    return t.stride(0), t.stride(1)
+
+
+@dataclass(frozen=True)
+class PlanInfo:
+    source_t: int
+    source_h: int
+    source_w: int
+    source_tokens: int
+    text_tokens: int
+    window_count: int
+    sequence_tokens: int
+    max_window_length: int
+    rope_dim: int
+    shifted: int
+    device: int
+
+
+class AwaPlan:
+    """Index maps, window table and RoPE table of one AWA layer configuration.
+
+    Arguments are the layers' ParamDict ids 0-8 (awa_layers.cpp:90-114, 872):
+    grid (``-1, -1, -1`` with ``runtime_spec`` = grid of the session), window
+    counts, text token count, shift flag and rotated feature count.
+    """
+
+    def __init__(self, source_t: int, source_h: int, source_w: int, windows_t: int, windows_h: int,
+                 windows_w: int, text_tokens: int = 58, shifted: bool = False, rope_dim: int = 126,
+                 runtime_spec: Optional[Tuple[int, int, int]] = None, host_only: bool = False):
+        lib = library()
+        params = _LayerParams(source_t, source_h, source_w, windows_t, windows_h, windows_w, text_tokens,
+                              int(bool(shifted)), rope_dim)
+        spec = None
+        if runtime_spec is not None:
+            t, h, w = runtime_spec
+            spec = _RuntimeSpec(t, h, w, t * h * w)
+        handle = ctypes.c_void_p()
+        create = lib.awa_plan_create_host if host_only else lib.awa_plan_create
+        rc = create(ctypes.byref(params), ctypes.byref(spec) if spec is not None else None, ctypes.byref(handle))
+        _check(rc)
+        self._handle = handle
+        info = _PlanInfo()
+        _check(lib.awa_plan_get_info(handle, ctypes.byref(info)))
+        self.info = PlanInfo(*(getattr(info, f[0]) for f in _PlanInfo._fields_))
+
+    def __del__(self):
+        handle = getattr(self, "_handle", None)
+        if handle and _lib is not None:
+            _lib.awa_plan_destroy(handle)
+            self._handle = None
+
+    @property
+    def handle(self):
+        return self._handle
+
+    def maps(self):
+        """Host copies of the index maps (numpy int32) and the window list."""
+        import numpy as np
+
+        inf = self.info
+        seq = np.empty(inf.sequence_tokens, np.int32)
+        cu = np.empty(inf.window_count + 1, np.int32)
+        vpos = np.empty(inf.source_tokens, np.int32)
+        tpos = np.empty(inf.window_count * inf.text_tokens, np.int32)
+        wins = (_Window * inf.window_count)()
+        _check(library().awa_plan_get_maps(self._handle, seq.ctypes.data, cu.ctypes.data, vpos.ctypes.data,
+                                           tpos.ctypes.data, ctypes.cast(wins, ctypes.c_void_p)))
+        return {"sequence_index": seq, "cu_seqlens": cu, "video_positions": vpos, "text_positions": tpos,
+                "windows": [(w.t0, w.t1, w.h0, w.h1, w.w0, w.w1) for w in wins]}
+
+    # ---------------------------------------------------------------- layers
+    def pack(self, video_qkv, text_qkv, out_dtype=None, stream=None):
+        """SeedVR2AWAPack: returns (packed [S, 3, H, d], cu_seqlens float [W+1])."""
+        torch = _torch()
+        heads, hd = video_qkv.shape[2], video_qkv.shape[3]
+        out_dtype = video_qkv.dtype if out_dtype is None else out_dtype
+        packed = torch.empty(self.info.sequence_tokens, 3, heads, hd, dtype=out_dtype, device=video_qkv.device)
+        cu = torch.empty(self.info.window_count + 1, dtype=torch.float32, device=video_qkv.device)
+        vts, vqs = _qkv_strides(video_qkv)
+        tts, tqs = _qkv_strides(text_qkv)
+        if video_qkv.dtype != text_qkv.dtype:
+            raise TypeError("video and text QKV must share a dtype")
+        _check(library().awa_pack(self._handle, heads, hd, _dtype_code(video_qkv), video_qkv.data_ptr(), vts, vqs,
+                                  text_qkv.data_ptr(), tts, tqs, _dtype_code(packed), packed.data_ptr(),
+                                  packed.stride(0), cu.data_ptr(), _stream_ptr(stream)))
+        return packed, cu
+
+    def mmrope(self, packed, out_dtype=None, stream=None):
+        """SeedVR2MMRoPE on a packed [S, 3, H, d] tensor."""
+        torch = _torch()
+        heads, hd = packed.shape[2], packed.shape[3]
+        out = torch.empty(packed.shape, dtype=packed.dtype if out_dtype is None else out_dtype, device=packed.device)
+        _check(library().awa_mmrope(self._handle, heads, hd, _dtype_code(packed), packed.data_ptr(), packed.stride(0),
+                                    _dtype_code(out), out.data_ptr(), out.stride(0), _stream_ptr(stream)))
+        return out
+
+    def window_attention(self, packed, precision=AWA_PREC_FP32, out_dtype=None, stream=None):
+        """SeedVR2WindowAttention: packed [S, 3, H, d] -> attended [S, H, d]."""
+        torch = _torch()
+        s, _, heads, hd = packed.shape
+        out = torch.empty(s, heads, hd, dtype=packed.dtype if out_dtype is None else out_dtype, device=packed.device)
+        _check(library().awa_window_attention(self._handle, precision, heads, hd, _dtype_code(packed),
+                                              packed.data_ptr(), packed.stride(0), _dtype_code(out), out.data_ptr(),
+                                              out.stride(0), _stream_ptr(stream)))
+        return out
+
+    def unpack(self, attended, out_dtype=None, stream=None):
+        """SeedVR2AWAUnpack: attended [S, H, d] -> (video [N_v, H, d], text [T, H, d])."""
+        torch = _torch()
+        _, heads, hd = attended.shape
+        dt = attended.dtype if out_dtype is None else out_dtype
+        video = torch.empty(self.info.source_tokens, heads, hd, dtype=dt, device=attended.device)
+        text = torch.empty(self.info.text_tokens, heads, hd, dtype=dt, device=attended.device)
+        _check(library().awa_unpack(self._handle, heads, hd, _dtype_code(attended), attended.data_ptr(),
+                                    attended.stride(0), _dtype_code(video), video.data_ptr(), video.stride(0),
+                                    text.data_ptr(), text.stride(0), _stream_ptr(stream)))
+        return video, text
+
+    # ---------------------------------------------------------------- fused chain
+    def workspace_bytes(self, heads: int, head_dim: int) -> int:
+        return int(library().awa_forward_workspace_bytes(self._handle, heads, head_dim))
+
+    def forward(self, video_qkv, text_qkv, precision=AWA_PREC_BF16, out_dtype=None, workspace=None,
+                video_out=None, text_out=None, stream=None):
+        """Pack -> MMRoPE -> WindowAttention -> Unpack in one pass: (video, text)."""
+        torch = _torch()
+        heads, hd = video_qkv.shape[2], video_qkv.shape[3]
+        dt = video_qkv.dtype if out_dtype is None else out_dtype
+        if video_out is None:
+            video_out = torch.empty(self.info.source_tokens, heads, hd, dtype=dt, device=video_qkv.device)
+        if text_out is None:
+            text_out = torch.empty(self.info.text_tokens, heads, hd, dtype=dt, device=video_qkv.device)
+        need = self.workspace_bytes(heads, hd)
+        if workspace is None:
+            workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=video_qkv.device)
+        vts, vqs = _qkv_strides(video_qkv)
+        tts, tqs = _qkv_strides(text_qkv)
+        _check(library().awa_forward(self._handle, precision, heads, hd, _dtype_code(video_qkv), video_qkv.data_ptr(),
+                                     vts, vqs, text_qkv.data_ptr(), tts, tqs, _dtype_code(video_out),
+                                     video_out.data_ptr(), video_out.stride(0), text_out.data_ptr(), text_out.stride(0),
+                                     workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+                                     _stream_ptr(stream)))
+        return video_out, text_out
+
+    def forward_windows(self, video_qkv, text_qkv, window_begin: int, window_end: int, video_out, text_partial,
+                        precision=AWA_PREC_BF16, workspace=None, stream=None):
+        """Windows [begin, end) only: writes their video rows and the fp32 text partial sum."""
+        torch = _torch()
+        heads, hd = video_qkv.shape[2], video_qkv.shape[3]
+        need = (window_end - window_begin) * self.info.text_tokens * heads * hd * 4
+        if workspace is None:
+            workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=video_qkv.device)
+        vts, vqs = _qkv_strides(video_qkv)
+        tts, tqs = _qkv_strides(text_qkv)
+        _check(library().awa_forward_windows(self._handle, precision, heads, hd, window_begin, window_end,
+                                             _dtype_code(video_qkv), video_qkv.data_ptr(), vts, vqs,
+                                             text_qkv.data_ptr(), tts, tqs, _dtype_code(video_out),
+                                             video_out.data_ptr(), video_out.stride(0), text_partial.data_ptr(),
+                                             workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+                                             _stream_ptr(stream)))
+
+    def text_finalize(self, text_sum, out_dtype, stream=None):
+        torch = _torch()
+        t, heads, hd = text_sum.shape
+        out = torch.empty(t, heads, hd, dtype=out_dtype, device=text_sum.device)
+        _check(library().awa_text_finalize(self._handle, heads, hd, text_sum.data_ptr(), _dtype_code(out),
+                                           out.data_ptr(), out.stride(0), _stream_ptr(stream)))
+        return out
+
+    def partition(self, parts: int) -> List[int]:
+        bounds = (ctypes.c_int * (parts + 1))()
+        _check(library().awa_partition_windows(self._handle, parts, ctypes.cast(bounds, ctypes.c_void_p)))
+        return list(bounds)
+
+    def range_video_rows(self, begin: int, end: int) -> int:
+        return int(library().awa_window_range_video_rows(self._handle, begin, end))
+
+    def gather_video_shard(self, video, begin: int, end: int, shard, stream=None):
+        _, heads, hd = video.shape
+        _check(library().awa_gather_video_shard(self._handle, heads, hd, begin, end, _dtype_code(video),
+                                                video.data_ptr(), video.stride(0), shard.data_ptr(),
+                                                _stream_ptr(stream)))
+
+    def scatter_video_shard(self, shard, begin: int, end: int, video, stream=None):
+        _, heads, hd = video.shape
+        _check(library().awa_scatter_video_shard(self._handle, heads, hd, begin, end, _dtype_code(video),
+                                                 shard.data_ptr(), video.data_ptr(), video.stride(0),
+                                                 _stream_ptr(stream)))
+
+    def attention_kernel_kind(self, precision: int, heads: int, head_dim: int) -> int:
+        return int(library().awa_attention_kernel_kind(self._handle, precision, heads, head_dim))
+
+
+def device_status() -> None:
+    """Raise if a device-side check of the library failed since the last call."""
+    _check(library().awa_device_status())
+
+
+def profile_enable(enabled: bool = True) -> None:
+    """Bracket every library kernel launch with CUDA events on its stream."""
+    library().awa_profile_enable(int(enabled))
+
+
+def profile_reset() -> None:
+    library().awa_profile_reset()
+
+
+def profile_collect() -> dict:
+    """{kernel name: (launches, total device ms)} since the last reset."""
+    lib = library()
+    n = lib.awa_profile_collect(None, 0)
+    buf = ctypes.create_string_buffer(n + 1)
+    lib.awa_profile_collect(buf, n + 1)
+    out = {}
+    for line in buf.value.decode().splitlines():
+        fields = dict(item.split("=", 1) for item in line.split()[1:])
+        out[fields["name"]] = (int(fields["launches"]), float(fields["ms"]))
+    return out
+
+
+# ---------------------------------------------------------------- ncnn layer classes
+_compat = None
+
+
+def ncnn_compat() -> ctypes.CDLL:
+    global _compat
+    if _compat is None:
+        library()
+        if not os.path.isfile(COMPAT_PATH):
+            raise ImportError(f"{COMPAT_PATH} is missing")
+        lib = ctypes.CDLL(COMPAT_PATH)
+        p, i = ctypes.c_void_p, ctypes.c_int
+        lib.awa_ncnn_run_chain.restype = i
+        lib.awa_ncnn_run_chain.argtypes = [p, i, i, i, i, i, i, i, p, p, p, p, p, p, p, p]
+        _compat = lib
+    return _compat
+
+
+def ncnn_run_chain(params: Sequence[int], heads: int, head_dim: int, video_qkv, text_qkv, layout: int = 0,
+                   runtime_spec: bool = False, bf16: bool = False, device_blobs: bool = False):
+    """Run SeedVR2AWAPack -> MMRoPE -> WindowAttention -> AWAUnpack through the
+    ncnn layer classes (register_seedvr2_awa_layers + Net + ParamDict + forward).
+
+    video_qkv / text_qkv: host numpy arrays [tokens, 3, H, d] (float32, or
+    uint16 holding bf16 bits). Returns a dict of dense numpy outputs.
+    """
+    import numpy as np
+
+    lib = ncnn_compat()
+    params = list(params)
+    elem = 2 if video_qkv.dtype == np.uint16 else 4
+    out_np = np.uint16 if bf16 else np.float32
+    n_v = params[0] * params[1] * params[2]
+    windows = make_windows(params[0:3], params[3:6], bool(params[7]))
+    s = n_v + len(windows) * params[6]
+    out = {
+        "packed": np.empty((s, 3, heads, head_dim), out_np),
+        "cu_seqlens": np.empty(len(windows) + 1, np.float32),
+        "roped": np.empty((s, 3, heads, head_dim), out_np),
+        "attended": np.empty((s, heads, head_dim), out_np),
+        "video": np.empty((n_v, heads, head_dim), out_np),
+        "text": np.empty((params[6], heads, head_dim), out_np),
+    }
+    arr = (ctypes.c_int * 9)(*params)
+    v = np.ascontiguousarray(video_qkv)
+    t = np.ascontiguousarray(text_qkv)
+    rc = lib.awa_ncnn_run_chain(ctypes.cast(arr, ctypes.c_void_p), heads, head_dim, layout, int(runtime_spec),
+                                int(bf16), int(device_blobs), elem, v.ctypes.data, t.ctypes.data,
+                                *(out[k].ctypes.data for k in ("packed", "cu_seqlens", "roped", "attended", "video",
+                                                               "text")))
+    out["status"] = rc
+    return out
+
+
+__all__ = ["AwaPlan", "AwaError", "PlanInfo", "library", "make_windows", "device_status", "ncnn_run_chain",
+           "EXPORTED_SYMBOLS", "AWA_F32", "AWA_BF16", "AWA_PREC_FP32", "AWA_PREC_BF16"]

@@ -1,0 +1,452 @@
+// awa_copy_kernels.cu -- the HBM-bound layers of the AWA chain:
+//   Pack      (awa_layers.cpp:419-458): gather source QKV rows into window order
+//   MMRoPE    (awa_layers.cpp:913-953): rotate Q/K features in interleaved pairs
+//   Unpack    (awa_layers.cpp:638-689): video rows back to source order, text mean
+// plus the text reduction of the fused path and the shard copies of the
+// multi-GPU path. Each thread moves 8 consecutive elements (16 or 32 bytes)
+// when rows allow it, so warps issue full-sector, coalesced accesses; grids
+// are sized in multiples of the SM count and stride over the work.
+#include "awa_device.cuh"
+#include "awa_internal.h"
+
+#include <cuda_bf16.h>
+
+namespace awa
+{
+namespace
+{
+
+using bf16 = __nv_bfloat16;
+
+int grid_for(int64_t work, int threads)
+{
+    static int sms = 0;
+    if (sms == 0)
+    {
+        int device = 0;
+        cudaGetDevice(&device);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        if (sms <= 0)
+            sms = 148;
+    }
+    const int64_t blocks = (work + threads - 1) / threads;
+    const int64_t cap = (int64_t)sms * 16;
+    return (int)(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+}
+
+bool aligned16(const void* p)
+{
+    return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+}
+
+// 8-element chunks are usable when every chunk start is 16-byte aligned.
+bool chunkable(int64_t row_elems, size_t elem, const void* const* ptrs, int nptr, const int64_t* strides, int nstride)
+{
+    if (row_elems % 8)
+        return false;
+    for (int i = 0; i < nptr; i++)
+        if (!aligned16(ptrs[i]))
+            return false;
+    for (int i = 0; i < nstride; i++)
+        if ((strides[i] * (int64_t)elem) % 16)
+            return false;
+    return true;
+}
+
+// ---------------------------------------------------------------- Pack
+template <typename TIn, typename TOut>
+__global__ void pack_chunks(PlanDevice plan, int head_row, const TIn* __restrict__ video, int64_t vts, int64_t vqs,
+                            const TIn* __restrict__ text, int64_t tts, int64_t tqs, TOut* __restrict__ packed,
+                            int64_t pts, float* __restrict__ cu_out)
+{
+    const int chunks_per_qkv = head_row / 8;
+    const int chunks_per_row = 3 * chunks_per_qkv;
+    const int64_t total = (int64_t)plan.sequence_tokens * chunks_per_row;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; id < total; id += step)
+    {
+        const int position = (int)(id / chunks_per_row);
+        const int c = (int)(id - (int64_t)position * chunks_per_row);
+        const int qkv = c / chunks_per_qkv;
+        const int e = (c - qkv * chunks_per_qkv) * 8;
+        const int source = __ldg(plan.sequence_index + position);
+        const TIn* src = source < plan.source_tokens
+                             ? video + (int64_t)source * vts + qkv * vqs + e
+                             : text + (int64_t)(source - plan.source_tokens) * tts + qkv * tqs + e;
+        float v[8];
+        load8(src, v);
+        store8(packed + (int64_t)position * pts + (int64_t)qkv * head_row + e, v);
+    }
+    if (cu_out && blockIdx.x == 0)
+        for (int i = threadIdx.x; i <= plan.window_count; i += blockDim.x)
+            cu_out[i] = (float)plan.cu_seqlens[i];  // cu_seqlens stored as float (awa_layers.cpp:455-456)
+}
+
+template <typename TIn, typename TOut>
+__global__ void pack_scalar(PlanDevice plan, int head_row, const TIn* __restrict__ video, int64_t vts, int64_t vqs,
+                            const TIn* __restrict__ text, int64_t tts, int64_t tqs, TOut* __restrict__ packed,
+                            int64_t pts, float* __restrict__ cu_out)
+{
+    const int row = 3 * head_row;
+    const int64_t total = (int64_t)plan.sequence_tokens * row;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; id < total; id += step)
+    {
+        const int position = (int)(id / row);
+        const int c = (int)(id - (int64_t)position * row);
+        const int qkv = c / head_row;
+        const int e = c - qkv * head_row;
+        const int source = __ldg(plan.sequence_index + position);
+        const TIn* src = source < plan.source_tokens
+                             ? video + (int64_t)source * vts + qkv * vqs + e
+                             : text + (int64_t)(source - plan.source_tokens) * tts + qkv * tqs + e;
+        store1(packed + (int64_t)position * pts + c, load1(src));
+    }
+    if (cu_out && blockIdx.x == 0)
+        for (int i = threadIdx.x; i <= plan.window_count; i += blockDim.x)
+            cu_out[i] = (float)plan.cu_seqlens[i];
+}
+
+// ---------------------------------------------------------------- MMRoPE
+// Bit-exact with the reference CPU forward in fp32: each product and the
+// difference/sum round separately (no FMA contraction), as the reference's
+// baseline x86-64 build does.
+__device__ __forceinline__ void rotate_pair(float x0, float x1, float c, float s, float& o0, float& o1)
+{
+    o0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+    o1 = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
+}
+
+__device__ __forceinline__ float2 rope_cs(const PlanDevice& plan, short4 coords, int pair)
+{
+    const int axis = pair / plan.pairs_per_axis;
+    const int within = pair - axis * plan.pairs_per_axis;
+    const int coord = axis == 0 ? coords.x : axis == 1 ? coords.y : coords.z;
+    return __ldg(plan.rope_table + coord * plan.pairs_per_axis + within);
+}
+
+template <typename TIn, typename TOut>
+__global__ void mmrope_chunks(PlanDevice plan, int heads, int head_dim, const TIn* __restrict__ in, int64_t its,
+                              TOut* __restrict__ out, int64_t ots)
+{
+    const int chunks_per_row = 3 * heads * head_dim / 8;
+    const int64_t total = (int64_t)plan.sequence_tokens * chunks_per_row;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    const short4* coords_table = reinterpret_cast<const short4*>(plan.position_coords);
+    for (int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; id < total; id += step)
+    {
+        const int position = (int)(id / chunks_per_row);
+        const int e = (int)(id - (int64_t)position * chunks_per_row) * 8;
+        const int qkv_head = e / head_dim;
+        const int f = e - qkv_head * head_dim;
+        float v[8];
+        load8(in + (int64_t)position * its + e, v);
+        if (qkv_head < 2 * heads && f < plan.rope_dim)
+        {
+            const short4 coords = coords_table[position];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+            {
+                if (f + 2 * i < plan.rope_dim)
+                {
+                    const float2 cs = rope_cs(plan, coords, (f >> 1) + i);
+                    rotate_pair(v[2 * i], v[2 * i + 1], cs.x, cs.y, v[2 * i], v[2 * i + 1]);
+                }
+            }
+        }
+        store8(out + (int64_t)position * ots + e, v);
+    }
+}
+
+template <typename TIn, typename TOut>
+__global__ void mmrope_scalar(PlanDevice plan, int heads, int head_dim, const TIn* __restrict__ in, int64_t its,
+                              TOut* __restrict__ out, int64_t ots)
+{
+    const int row = 3 * heads * head_dim;
+    const int64_t total = (int64_t)plan.sequence_tokens * row;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    const short4* coords_table = reinterpret_cast<const short4*>(plan.position_coords);
+    for (int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; id < total; id += step)
+    {
+        const int position = (int)(id / row);
+        const int e = (int)(id - (int64_t)position * row);
+        const int qkv_head = e / head_dim;
+        const int f = e - qkv_head * head_dim;
+        const TIn* src = in + (int64_t)position * its;
+        float value = load1(src + e);
+        if (qkv_head < 2 * heads && f < plan.rope_dim)
+        {
+            const float2 cs = rope_cs(plan, coords_table[position], f >> 1);
+            const float paired = load1(src + (f & 1 ? e - 1 : e + 1));
+            float o0, o1;
+            if (f & 1)
+                rotate_pair(paired, value, cs.x, cs.y, o0, o1), value = o1;
+            else
+                rotate_pair(value, paired, cs.x, cs.y, o0, o1), value = o0;
+        }
+        store1(out + (int64_t)position * ots + e, value);
+    }
+}
+
+// ---------------------------------------------------------------- Unpack
+template <typename TIn, typename TOut>
+__global__ void unpack_video_chunks(PlanDevice plan, int head_row, const TIn* __restrict__ attended, int64_t its,
+                                   TOut* __restrict__ video, int64_t vts)
+{
+    const int chunks_per_row = head_row / 8;
+    const int64_t total = (int64_t)plan.source_tokens * chunks_per_row;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; id < total; id += step)
+    {
+        const int token = (int)(id / chunks_per_row);
+        const int e = (int)(id - (int64_t)token * chunks_per_row) * 8;
+        const int position = __ldg(plan.video_positions + token);
+        float v[8];
+        load8(attended + (int64_t)position * its + e, v);
+        store8(video + (int64_t)token * vts + e, v);
+    }
+}
+
+template <typename TIn, typename TOut>
+__global__ void unpack_video_scalar(PlanDevice plan, int head_row, const TIn* __restrict__ attended, int64_t its,
+                                    TOut* __restrict__ video, int64_t vts)
+{
+    const int64_t total = (int64_t)plan.source_tokens * head_row;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; id < total; id += step)
+    {
+        const int token = (int)(id / head_row);
+        const int e = (int)(id - (int64_t)token * head_row);
+        const int position = __ldg(plan.video_positions + token);
+        store1(video + (int64_t)token * vts + e, load1(attended + (int64_t)position * its + e));
+    }
+}
+
+// Text rows: out[i][e] = sum over windows (in order) of src(w, i)[e] / divisor,
+// one thread per element, sequential over windows as the CPU forward
+// (awa_layers.cpp:677-687), so the sum is bit-identical for identical inputs.
+template <typename TIn, typename TOut>
+__global__ void text_reduce(PlanDevice plan, int head_row, int packed, const TIn* __restrict__ src, int64_t sts,
+                            int window_begin, int window_end, float divisor, TOut* __restrict__ out, int64_t ots)
+{
+    const int text = plan.text_tokens;
+    const int64_t total = (int64_t)text * head_row;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; id < total; id += step)
+    {
+        const int i = (int)(id / head_row);
+        const int e = (int)(id - (int64_t)i * head_row);
+        float acc = 0.f;
+        for (int w = window_begin; w < window_end; w++)
+        {
+            const int64_t row = packed ? (int64_t)__ldg(plan.cu_seqlens + w + 1) - text + i
+                                       : (int64_t)(w - window_begin) * text + i;
+            const float x = load1(src + row * sts + e);
+            acc = __fadd_rn(acc, divisor != 0.f ? __fdiv_rn(x, divisor) : x);
+        }
+        store1(out + (int64_t)i * ots + e, acc);
+    }
+}
+
+template <typename TOut>
+__global__ void text_scale(int rows, int head_row, const float* __restrict__ sum, float divisor, TOut* __restrict__ out,
+                           int64_t ots)
+{
+    const int64_t total = (int64_t)rows * head_row;
+    for (int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; id < total; id += (int64_t)gridDim.x * blockDim.x)
+    {
+        const int i = (int)(id / head_row);
+        const int e = (int)(id - (int64_t)i * head_row);
+        store1(out + (int64_t)i * ots + e, __fdiv_rn(sum[id], divisor));
+    }
+}
+
+// Video rows of windows [begin, end) between source order and the dense
+// shard order (window by window, video rows only). One block per window.
+template <typename T>
+__global__ void shard_copy_kernel(PlanDevice plan, int head_row, int window_begin, const T* __restrict__ src,
+                                  int64_t src_stride, T* __restrict__ dst, int64_t dst_stride, int to_source)
+{
+    const int w = window_begin + blockIdx.x;
+    const WindowDesc win = plan.windows[w];
+    const int64_t shard_base = (int64_t)(plan.cu_seqlens[w] - plan.cu_seqlens[window_begin]) -
+                               (int64_t)(w - window_begin) * plan.text_tokens;
+    const int plane = win.nh * win.nw;
+    const int64_t total = (int64_t)win.video * head_row;
+    for (int64_t id = threadIdx.x; id < total; id += blockDim.x)
+    {
+        const int r = (int)(id / head_row);
+        const int e = (int)(id - (int64_t)r * head_row);
+        const int t = win.t0 + r / plane;
+        const int h = win.h0 + (r % plane) / win.nw;
+        const int x = win.w0 + r % win.nw;
+        const int64_t token = ((int64_t)t * plan.source_h + h) * plan.source_w + x;
+        const int64_t shard_row = shard_base + r;
+        if (to_source)
+            dst[token * dst_stride + e] = src[shard_row * src_stride + e];
+        else
+            dst[shard_row * dst_stride + e] = src[token * src_stride + e];
+    }
+}
+
+template <template <typename, typename> class Fn, typename... Args>
+int dispatch2(int in_dtype, int out_dtype, Args&&... args)
+{
+    if (in_dtype == kF32 && out_dtype == kF32)
+        return Fn<float, float>::run(args...);
+    if (in_dtype == kF32 && out_dtype == kBF16)
+        return Fn<float, bf16>::run(args...);
+    if (in_dtype == kBF16 && out_dtype == kF32)
+        return Fn<bf16, float>::run(args...);
+    return Fn<bf16, bf16>::run(args...);
+}
+
+template <typename TIn, typename TOut>
+struct PackLaunch
+{
+    static int run(const PlanDevice& plan, int heads, int head_dim, const void* video, int64_t vts, int64_t vqs,
+                   const void* text, int64_t tts, int64_t tqs, void* packed, int64_t pts, float* cu_out,
+                   cudaStream_t stream)
+    {
+        const int head_row = heads * head_dim;
+        const void* ptrs[3] = {video, text, packed};
+        const int64_t in_strides[4] = {vts, vqs, tts, tqs};
+        const bool vec = chunkable(head_row, sizeof(TIn), ptrs, 2, in_strides, 4) &&
+                         chunkable(head_row, sizeof(TOut), ptrs + 2, 1, &pts, 1);
+        const int threads = 256;
+        if (vec)
+            pack_chunks<TIn, TOut><<<grid_for((int64_t)plan.sequence_tokens * 3 * head_row / 8, threads), threads, 0,
+                                     stream>>>(plan, head_row, (const TIn*)video, vts, vqs, (const TIn*)text, tts, tqs,
+                                               (TOut*)packed, pts, cu_out);
+        else
+            pack_scalar<TIn, TOut><<<grid_for((int64_t)plan.sequence_tokens * 3 * head_row, threads), threads, 0,
+                                     stream>>>(plan, head_row, (const TIn*)video, vts, vqs, (const TIn*)text, tts, tqs,
+                                               (TOut*)packed, pts, cu_out);
+        return (int)cudaGetLastError();
+    }
+};
+
+template <typename TIn, typename TOut>
+struct MmropeLaunch
+{
+    static int run(const PlanDevice& plan, int heads, int head_dim, const void* in, int64_t its, void* out, int64_t ots,
+                   cudaStream_t stream)
+    {
+        const void* pin[1] = {in};
+        const void* pout[1] = {out};
+        const bool vec = head_dim % 8 == 0 && chunkable(3 * heads * head_dim, sizeof(TIn), pin, 1, &its, 1) &&
+                         chunkable(3 * heads * head_dim, sizeof(TOut), pout, 1, &ots, 1);
+        const int threads = 256;
+        if (vec)
+            mmrope_chunks<TIn, TOut><<<grid_for((int64_t)plan.sequence_tokens * 3 * heads * head_dim / 8, threads),
+                                       threads, 0, stream>>>(plan, heads, head_dim, (const TIn*)in, its, (TOut*)out, ots);
+        else
+            mmrope_scalar<TIn, TOut><<<grid_for((int64_t)plan.sequence_tokens * 3 * heads * head_dim, threads), threads,
+                                       0, stream>>>(plan, heads, head_dim, (const TIn*)in, its, (TOut*)out, ots);
+        return (int)cudaGetLastError();
+    }
+};
+
+template <typename TIn, typename TOut>
+struct UnpackVideoLaunch
+{
+    static int run(const PlanDevice& plan, int heads, int head_dim, const void* attended, int64_t its, void* video,
+                   int64_t vts, cudaStream_t stream)
+    {
+        const int head_row = heads * head_dim;
+        const void* pin[1] = {attended};
+        const void* pout[1] = {video};
+        const bool vec = chunkable(head_row, sizeof(TIn), pin, 1, &its, 1) &&
+                         chunkable(head_row, sizeof(TOut), pout, 1, &vts, 1);
+        const int threads = 256;
+        if (vec)
+            unpack_video_chunks<TIn, TOut><<<grid_for((int64_t)plan.source_tokens * head_row / 8, threads), threads, 0,
+                                             stream>>>(plan, head_row, (const TIn*)attended, its, (TOut*)video, vts);
+        else
+            unpack_video_scalar<TIn, TOut><<<grid_for((int64_t)plan.source_tokens * head_row, threads), threads, 0,
+                                             stream>>>(plan, head_row, (const TIn*)attended, its, (TOut*)video, vts);
+        return (int)cudaGetLastError();
+    }
+};
+
+template <typename TIn, typename TOut>
+struct TextReduceLaunch
+{
+    static int run(const PlanDevice& plan, int heads, int head_dim, int packed, const void* src, int64_t sts,
+                   int window_begin, int window_end, float divisor, void* out, int64_t ots, cudaStream_t stream)
+    {
+        const int head_row = heads * head_dim;
+        const int threads = 256;
+        text_reduce<TIn, TOut><<<grid_for((int64_t)plan.text_tokens * head_row, threads), threads, 0, stream>>>(
+            plan, head_row, packed, (const TIn*)src, sts, window_begin, window_end, divisor, (TOut*)out, ots);
+        return (int)cudaGetLastError();
+    }
+};
+
+}  // namespace
+
+int launch_pack(const PlanDevice& plan, int heads, int head_dim, int in_dtype, const void* video, int64_t vts,
+                int64_t vqs, const void* text, int64_t tts, int64_t tqs, int out_dtype, void* packed, int64_t pts,
+                float* cu_out, cudaStream_t stream)
+{
+    ProfileScope prof("awa_pack", stream);
+    return dispatch2<PackLaunch>(in_dtype, out_dtype, plan, heads, head_dim, video, vts, vqs, text, tts, tqs, packed,
+                                 pts, cu_out, stream);
+}
+
+int launch_mmrope(const PlanDevice& plan, int heads, int head_dim, int in_dtype, const void* in, int64_t its,
+                  int out_dtype, void* out, int64_t ots, cudaStream_t stream)
+{
+    ProfileScope prof("awa_mmrope", stream);
+    return dispatch2<MmropeLaunch>(in_dtype, out_dtype, plan, heads, head_dim, in, its, out, ots, stream);
+}
+
+int launch_unpack_video(const PlanDevice& plan, int heads, int head_dim, int in_dtype, const void* attended,
+                        int64_t its, int out_dtype, void* video, int64_t vts, cudaStream_t stream)
+{
+    ProfileScope prof("awa_unpack_video", stream);
+    return dispatch2<UnpackVideoLaunch>(in_dtype, out_dtype, plan, heads, head_dim, attended, its, video, vts, stream);
+}
+
+int launch_text_reduce(const PlanDevice& plan, int heads, int head_dim, int packed, int in_dtype, const void* src,
+                       int64_t src_token_stride, int window_begin, int window_end, float divisor, int out_dtype,
+                       void* text_out, int64_t text_token_stride, cudaStream_t stream)
+{
+    ProfileScope prof("awa_text_reduce", stream);
+    return dispatch2<TextReduceLaunch>(in_dtype, out_dtype, plan, heads, head_dim, packed, src, src_token_stride,
+                                       window_begin, window_end, divisor, text_out, text_token_stride, stream);
+}
+
+int launch_text_scale(int rows, int heads, int head_dim, const float* text_sum, float divisor, int out_dtype,
+                      void* text_out, int64_t text_token_stride, cudaStream_t stream)
+{
+    ProfileScope prof("awa_text_scale", stream);
+    const int head_row = heads * head_dim;
+    const int threads = 256;
+    const int grid = grid_for((int64_t)rows * head_row, threads);
+    if (out_dtype == kF32)
+        text_scale<float><<<grid, threads, 0, stream>>>(rows, head_row, text_sum, divisor, (float*)text_out,
+                                                        text_token_stride);
+    else
+        text_scale<bf16><<<grid, threads, 0, stream>>>(rows, head_row, text_sum, divisor, (bf16*)text_out,
+                                                       text_token_stride);
+    return (int)cudaGetLastError();
+}
+
+int launch_shard_copy(const PlanDevice& plan, int heads, int head_dim, int window_begin, int window_end, int dtype,
+                      const void* src, int64_t src_stride, void* dst, int64_t dst_stride, int to_source,
+                      cudaStream_t stream)
+{
+    ProfileScope prof("awa_shard_copy", stream);
+    const int head_row = heads * head_dim;
+    const int blocks = window_end - window_begin;
+    if (dtype == kF32)
+        shard_copy_kernel<float><<<blocks, 256, 0, stream>>>(plan, head_row, window_begin, (const float*)src, src_stride,
+                                                             (float*)dst, dst_stride, to_source);
+    else
+        shard_copy_kernel<bf16><<<blocks, 256, 0, stream>>>(plan, head_row, window_begin, (const bf16*)src, src_stride,
+                                                            (bf16*)dst, dst_stride, to_source);
+    return (int)cudaGetLastError();
+}
+
+}  // namespace awa

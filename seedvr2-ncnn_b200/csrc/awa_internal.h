@@ -1,0 +1,145 @@
+// awa_internal.h -- structures shared by the host plan (awa_plan.cpp) and the
+// CUDA kernels (awa_copy_kernels.cu, awa_attn_simt.cu, awa_attn_tc.cu).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+namespace awa
+{
+
+// One window of the plan, in make_windows order. Rows of a window are its
+// video tokens in (t, h, w) row-major order, then the text tokens: the
+// packed order of SeedVR2AWAPack (awa_layers.cpp:391-407).
+struct WindowDesc
+{
+    int t0, h0, w0;  // clipped start (origin of the window-local RoPE coordinates)
+    int nt, nh, nw;  // clipped extent
+    int offset;      // first packed row (cu_seqlens[w])
+    int video;       // nt * nh * nw
+};
+
+// Device tables of a plan (uploaded once by awa_plan_create).
+struct PlanDevice
+{
+    const WindowDesc* windows = nullptr;
+    const int* sequence_index = nullptr;   // [S]
+    const int* cu_seqlens = nullptr;       // [W+1]
+    const int* video_positions = nullptr;  // [N_v]
+    const int* position_coords = nullptr;  // [S] short4 RoPE coordinates (t, h, w, 0) per packed row
+    const float2* rope_table = nullptr;    // [max_coord][pairs_per_axis] (cos, sin)
+    int source_t = 0, source_h = 0, source_w = 0;
+    int source_tokens = 0;
+    int text_tokens = 0;
+    int window_count = 0;
+    int sequence_tokens = 0;
+    int rope_dim = 0;
+    int pairs_per_axis = 0;  // rope_dim / 6
+    int max_coord = 0;
+};
+
+enum DType : int
+{
+    kF32 = 0,
+    kBF16 = 1
+};
+
+// Where an attention kernel reads its rows and writes its outputs.
+//  packed mode: rows of window w are packed rows cu[w] .. cu[w+1]-1 of `qkv`
+//               (q heads, k heads, v heads per row); outputs go to packed rows
+//               of `out`. RoPE already applied (by the MMRoPE layer).
+//  fused mode:  rows are gathered from the source QKV (video rows by window
+//               geometry, text rows from the text QKV), Q/K are rotated on the
+//               fly; video outputs go to source-order rows of `out`, text
+//               outputs to `text_partial` [W][text][H][d] (fp32).
+struct AttnArgs
+{
+    PlanDevice plan;
+    int heads = 0;
+    int head_dim = 0;
+    float scale = 0.f;       // 1/sqrt(head_dim), as the reference computes it
+    // packed mode
+    const void* qkv = nullptr;
+    int64_t qkv_token_stride = 0;
+    // fused mode
+    const void* video_qkv = nullptr;
+    int64_t video_token_stride = 0, video_qkv_stride = 0;
+    const void* text_qkv = nullptr;
+    int64_t text_token_stride = 0, text_qkv_stride = 0;
+    // outputs
+    void* out = nullptr;
+    int64_t out_token_stride = 0;
+    float* text_partial = nullptr;  // fused: [window - window_begin][text][H][d]
+    // work list: (window, q tile) items, grid.y = heads
+    const int2* items = nullptr;
+    int item_count = 0;
+    int window_begin = 0;  // fused, sharded: first window of this launch
+    int* error_flag = nullptr;
+};
+
+// Launchers (return a cudaError_t value as int).
+int launch_pack(const PlanDevice& plan, int heads, int head_dim, int in_dtype, const void* video, int64_t vts,
+                int64_t vqs, const void* text, int64_t tts, int64_t tqs, int out_dtype, void* packed, int64_t pts,
+                float* cu_out, cudaStream_t stream);
+int launch_mmrope(const PlanDevice& plan, int heads, int head_dim, int in_dtype, const void* in, int64_t its,
+                  int out_dtype, void* out, int64_t ots, cudaStream_t stream);
+int launch_unpack_video(const PlanDevice& plan, int heads, int head_dim, int in_dtype, const void* attended,
+                        int64_t its, int out_dtype, void* video, int64_t vts, cudaStream_t stream);
+// text_out[i] = sum_w src(w, i) / divisor in window order; src(w, i) is either
+// packed row cu[w+1]-text+i of `attended` (packed != 0) or row (w*text+i) of a
+// dense fp32 [W][text][H*d] array. If divisor == 0 the sum is not divided and
+// the result is written as fp32 (partial sums).
+int launch_text_reduce(const PlanDevice& plan, int heads, int head_dim, int packed, int in_dtype, const void* src,
+                       int64_t src_token_stride, int window_begin, int window_end, float divisor, int out_dtype,
+                       void* text_out, int64_t text_token_stride, cudaStream_t stream);
+int launch_text_scale(int rows, int heads, int head_dim, const float* text_sum, float divisor, int out_dtype,
+                      void* text_out, int64_t text_token_stride, cudaStream_t stream);
+int launch_shard_copy(const PlanDevice& plan, int heads, int head_dim, int window_begin, int window_end, int dtype,
+                      const void* src, int64_t src_stride, void* dst, int64_t dst_stride, int to_source,
+                      cudaStream_t stream);
+
+// Attention: packed != 0 selects packed mode. Template dispatch on dtypes.
+int launch_attention_simt(const AttnArgs& args, int packed, int in_dtype, int out_dtype, cudaStream_t stream);
+int launch_attention_tc(const AttnArgs& args, int packed, int in_dtype, int out_dtype, cudaStream_t stream);
+
+int* device_error_flag();  // per-device flag in device memory
+
+// Launch profiler: ProfileScope brackets one launch with events when enabled.
+bool profiling_enabled();
+void profile_record(const char* name, cudaEvent_t start, cudaEvent_t stop);
+cudaEvent_t profile_event();
+struct ProfileScope
+{
+    const char* name;
+    cudaStream_t stream;
+    cudaEvent_t start = nullptr;
+    ProfileScope(const char* kernel, cudaStream_t s) : name(kernel), stream(s)
+    {
+        if (profiling_enabled())
+        {
+            start = profile_event();
+            if (start)
+                cudaEventRecord(start, stream);
+        }
+    }
+    ~ProfileScope()
+    {
+        if (start)
+        {
+            cudaEvent_t stop = profile_event();
+            if (stop)
+            {
+                cudaEventRecord(stop, stream);
+                profile_record(name, start, stop);
+            }
+        }
+    }
+};
+
+constexpr int kTcRowsPerTile = 128;   // query rows of one tcgen05 work item
+constexpr int kSimtRowsPerTile = 64;  // query rows of one SIMT work item
+constexpr int kMaxHeadDim = 128;
+
+}  // namespace awa
