@@ -78,10 +78,22 @@ class Oracle:
         if not os.path.isfile(path):
             build(reference=False)
         lib = ctypes.CDLL(path)
-        lib.oracle_make_windows.restype = _i
-        lib.oracle_index_maps.restype = _i
-        lib.oracle_rope_table.restype = _i
-        lib.oracle_unpack.restype = _i
+        i7 = [_i] * 7
+        sig = {
+            "oracle_make_windows": (_i, i7 + [_p, _i]),
+            "oracle_index_maps": (_i, i7 + [_i, _p, _p, _p, _p]),
+            "oracle_pack": (None, [_p, _p, _i, _i, _i, _p, _i, _p]),
+            "oracle_rope_table": (_i, i7 + [_i, _i, _p]),
+            "oracle_rope": (None, [_p, _i, _i, _i, _i, _p, _p]),
+            "oracle_attention": (None, [_p, _i, _p, _i, _i, _p, _i]),
+            "oracle_attention_range": (None, [_p, _i, _i, _p, _i, _i, _p, _i]),
+            "oracle_unpack": (_i, [_p, _i, _i, _i, _i, _i, _i, _p, _p, _p, _p]),
+            "oracle_round_bf16": (None, [_p, _p, ctypes.c_int64]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
         self.lib = lib
 
     def make_windows(self, size: Sequence[int], num: Sequence[int], shifted: bool) -> List[Tuple[int, ...]]:
@@ -138,9 +150,19 @@ class Oracle:
         assert rc == maps_len
         return table
 
+    def rope(self, packed: np.ndarray, table: np.ndarray, heads: int, head_dim: int, rope_dim: int) -> np.ndarray:
+        """MMRoPE of packed rows [n, 3, H, d] with their table rows [n, 2*rope_dim]."""
+        packed = np.ascontiguousarray(packed, dtype=np.float32)
+        table = np.ascontiguousarray(table, dtype=np.float32)
+        out = np.empty_like(packed)
+        self.lib.oracle_rope(_ptr(packed), packed.shape[0], heads, head_dim, rope_dim, _ptr(table), _ptr(out))
+        return out
+
     def attention_range(self, packed: np.ndarray, cu: np.ndarray, first: int, last: int, heads: int, head_dim: int,
                         attended: np.ndarray, threads: int = 1) -> None:
         cu = np.ascontiguousarray(cu, dtype=np.int32)
+        packed = np.ascontiguousarray(packed, dtype=np.float32)
+        assert attended.flags["C_CONTIGUOUS"] and attended.dtype == np.float32
         self.lib.oracle_attention_range(_ptr(packed), first, last, _ptr(cu), heads, head_dim, _ptr(attended), threads)
 
     def round_bf16(self, x: np.ndarray) -> np.ndarray:

@@ -30,6 +30,7 @@ struct PlanDevice
     const int* video_positions = nullptr;  // [N_v]
     const int* position_coords = nullptr;  // [S] short4 RoPE coordinates (t, h, w, 0) per packed row
     const float2* rope_table = nullptr;    // [max_coord][pairs_per_axis] (cos, sin)
+    const uint32_t* rope_table_bf16 = nullptr; // same entries as bf16 pairs (cos low, sin high)
     int source_t = 0, source_h = 0, source_w = 0;
     int source_tokens = 0;
     int text_tokens = 0;
@@ -72,7 +73,8 @@ struct AttnArgs
     void* out = nullptr;
     int64_t out_token_stride = 0;
     float* text_partial = nullptr;  // fused: [window - window_begin][text][H][d]
-    // work list: (window, q tile) items, grid.y = heads
+    // work list: (window, q tile) items (SIMT: 64-row tiles; tcgen05: pairs of
+    // 128-row tiles), each taken for every head
     const int2* items = nullptr;
     int item_count = 0;
     int window_begin = 0;  // fused, sharded: first window of this launch
@@ -138,7 +140,7 @@ struct ProfileScope
     }
 };
 
-constexpr int kTcRowsPerTile = 128;   // query rows of one tcgen05 work item
+constexpr int kTcRowsPerTile = 128;   // query rows of one tcgen05 tile (a work item holds two)
 constexpr int kSimtRowsPerTile = 64;  // query rows of one SIMT work item
 constexpr int kMaxHeadDim = 128;
 

@@ -32,8 +32,9 @@ struct awa_plan
     std::vector<int> video_positions;
     std::vector<int> text_positions;
     std::vector<float2> rope_table;
+    std::vector<uint32_t> rope_table_bf16;  // per (coord, pair): bf16 cos (low half), bf16 sin (high half)
     std::vector<short4> position_coords;
-    std::vector<int2> items_tc;    // (window, 128-row q tile), longest windows first
+    std::vector<int2> items_tc;    // (window, pair of 128-row q tiles), longest windows first
     std::vector<int2> items_simt;  // (window, 64-row q tile)
     std::vector<int> item_window_begin_tc;  // items_tc index of the first item of each window (plan order)
     std::vector<double> window_cost;        // L^2 per window
@@ -123,6 +124,17 @@ std::vector<awa_window> build_windows(int st, int sh, int sw, int nt, int nh, in
                     out.push_back(win);
             }
     return out;
+}
+
+// Two floats rounded to bf16 (nearest even), packed low/high.
+uint32_t bf16_pair(float lo, float hi)
+{
+    auto round = [](float f) -> uint32_t {
+        uint32_t bits;
+        std::memcpy(&bits, &f, 4);
+        return (bits + 0x7fffu + ((bits >> 16) & 1u)) >> 16;
+    };
+    return round(lo) | (round(hi) << 16);
 }
 
 template <typename T>
@@ -341,13 +353,16 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
     plan->max_coord = max_coord;
     const int axis_dim = rope_dim / 3;
     plan->rope_table.resize((size_t)max_coord * plan->pairs_per_axis);
+    plan->rope_table_bf16.resize(plan->rope_table.size());
     for (int pair = 0; pair < plan->pairs_per_axis; pair++)
     {
         const float frequency = std::pow(10000.f, -static_cast<float>(2 * pair) / axis_dim);
         for (int coord = 0; coord < max_coord; coord++)
         {
             const float angle = coord * frequency;
-            plan->rope_table[(size_t)coord * plan->pairs_per_axis + pair] = make_float2(std::cos(angle), std::sin(angle));
+            const float c = std::cos(angle), sn = std::sin(angle);
+            plan->rope_table[(size_t)coord * plan->pairs_per_axis + pair] = make_float2(c, sn);
+            plan->rope_table_bf16[(size_t)coord * plan->pairs_per_axis + pair] = bf16_pair(c, sn);
         }
     }
 
@@ -359,7 +374,7 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
     for (int w : order)
     {
         const int length = plan->descs[w].video + text;
-        for (int q = 0; q < ceil_div(length, awa::kTcRowsPerTile); q++)
+        for (int q = 0; q < ceil_div(length, 2 * awa::kTcRowsPerTile); q++)
             plan->items_tc.push_back(make_int2(w, q));
         for (int q = 0; q < ceil_div(length, awa::kSimtRowsPerTile); q++)
             plan->items_simt.push_back(make_int2(w, q));
@@ -393,7 +408,7 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
     size_t total = 0;
     const size_t sizes[9] = {bytes_of(plan->descs),        bytes_of(plan->sequence_index),  bytes_of(plan->cu_seqlens),
                              bytes_of(plan->video_positions), bytes_of(plan->position_coords), bytes_of(plan->rope_table),
-                             bytes_of(plan->items_tc),     bytes_of(plan->items_simt),      0};
+                             bytes_of(plan->items_tc),     bytes_of(plan->items_simt),      bytes_of(plan->rope_table_bf16)};
     for (int i = 0; i < 9; i++)
     {
         offsets[i] = total;
@@ -406,10 +421,10 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
         return cuda_fail(err, "cudaMalloc(plan tables)");
     }
     std::vector<unsigned char> staging(total, 0);
-    const void* sources[8] = {plan->descs.data(),           plan->sequence_index.data(), plan->cu_seqlens.data(),
+    const void* sources[9] = {plan->descs.data(),           plan->sequence_index.data(), plan->cu_seqlens.data(),
                               plan->video_positions.data(), plan->position_coords.data(), plan->rope_table.data(),
-                              plan->items_tc.data(),        plan->items_simt.data()};
-    for (int i = 0; i < 8; i++)
+                              plan->items_tc.data(),        plan->items_simt.data(),      plan->rope_table_bf16.data()};
+    for (int i = 0; i < 9; i++)
         if (sizes[i])
             std::memcpy(staging.data() + offsets[i], sources[i], sizes[i]);
     err = cudaMemcpy(plan->device_block, staging.data(), total, cudaMemcpyHostToDevice);
@@ -427,6 +442,7 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
     dev.video_positions = reinterpret_cast<const int*>(base + offsets[3]);
     dev.position_coords = reinterpret_cast<const int*>(base + offsets[4]);
     dev.rope_table = reinterpret_cast<const float2*>(base + offsets[5]);
+    dev.rope_table_bf16 = reinterpret_cast<const uint32_t*>(base + offsets[8]);
     plan->d_items_tc = reinterpret_cast<const int2*>(base + offsets[6]);
     plan->d_items_simt = reinterpret_cast<const int2*>(base + offsets[7]);
     dev.source_t = st;
@@ -539,9 +555,11 @@ int awa_mmrope(const awa_plan* plan, int heads, int head_dim, int in_dtype, cons
 
 int awa_attention_kernel_kind(const awa_plan* plan, int precision, int heads, int head_dim)
 {
-    (void)plan;
     (void)heads;
-    return precision == AWA_PREC_BF16 && head_dim == 128 ? 1 : 2;
+    // The tcgen05 kernel keeps the (coordinate, pair) RoPE table in 16 KB of
+    // shared memory: 4096 entries, i.e. window extents up to ~195 at rope_dim 126.
+    const bool table_fits = plan && (long long)plan->max_coord * plan->pairs_per_axis <= 4096;
+    return precision == AWA_PREC_BF16 && head_dim == 128 && table_fits ? 1 : 2;
 }
 
 static int run_attention(const awa_plan* plan, int precision, awa::AttnArgs& args, int packed, int in_dtype,

@@ -68,9 +68,7 @@ def test_full_layer(name, cfg, precision, oracle):
         src[~is_video] = t[seq_t[~is_video] - cfg.source_tokens].float()
         packed_w = np.ascontiguousarray(to_host(src))
         assert np.array_equal(to_host(packed32[cu[w]:cu[w + 1]]), packed_w)
-        roped_w = np.empty_like(packed_w)
-        oracle.lib.oracle_rope(packed_w.ctypes.data, len(rows), cfg.heads, cfg.head_dim, cfg.rope_dim,
-                               np.ascontiguousarray(table[rows]).ctypes.data, roped_w.ctypes.data)
+        roped_w = oracle.rope(packed_w, table[rows], cfg.heads, cfg.head_dim, cfg.rope_dim)
         assert np.array_equal(to_host(roped32[cu[w]:cu[w + 1]]), roped_w)
         att_w = np.empty((len(rows), cfg.heads, cfg.head_dim), np.float32)
         oracle.attention_range(roped_w, np.array([0, len(rows)], np.int32), 0, 1, cfg.heads, cfg.head_dim, att_w,
