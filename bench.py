@@ -221,7 +221,7 @@ def run_b200(args, rank, world, local_rank):
     flops = attention_flops(lengths)
     n_v = grid[0] * grid[1] * grid[2]
     plan = awa_b200.AwaPlan(*grid, *num, text_tokens=TEXT, shifted=bool(shifted))
-    kernel_kind = plan.attention_kernel_kind(prec, HEADS, HEAD_DIM)
+    kernel_kind = plan.attention_kernel_kind(prec, HEADS, HEAD_DIM, dtype)
 
     gen = torch.Generator(device=device).manual_seed(1234 + rank)
     video_qkv = torch.randn(n_v, 3, HEADS, HEAD_DIM, device=device, generator=gen).to(dtype)

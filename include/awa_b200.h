@@ -192,8 +192,10 @@ int awa_partition_windows(const awa_plan* plan, int parts, int* bounds);
 int awa_device_status(void);
 
 /* Which attention kernel awa_window_attention / awa_forward would launch for
- * these arguments: 1 = tcgen05 (sm_100a tensor cores), 2 = fp32 SIMT. */
-int awa_attention_kernel_kind(const awa_plan* plan, int precision, int heads, int head_dim);
+ * these arguments: 1 = tcgen05 (sm_100a tensor cores: AWA_PREC_BF16 with bf16
+ * inputs and head_dim 128), 2 = fp32 SIMT (everything else; fp32 inputs at
+ * AWA_PREC_BF16 are computed in fp32, which is within the bf16 tolerance). */
+int awa_attention_kernel_kind(const awa_plan* plan, int precision, int in_dtype, int heads, int head_dim);
 
 /* Opt-in launch profiler (the counterpart of the reference's
  * PerformanceProfile, src/inference/performance_profile.h:75-227): while

@@ -98,7 +98,7 @@ def library() -> ctypes.CDLL:
         "awa_window_range_video_rows": (i64, [p, i, i]),
         "awa_partition_windows": (i, [p, i, p]),
         "awa_device_status": (i, []),
-        "awa_attention_kernel_kind": (i, [p, i, i, i]),
+        "awa_attention_kernel_kind": (i, [p, i, i, i, i]),
         "awa_profile_enable": (None, [i]),
         "awa_profile_reset": (None, []),
         "awa_profile_collect": (i, [p, sz]),
@@ -347,8 +347,14 @@ class AwaPlan:
                                                  shard.data_ptr(), video.data_ptr(), video.stride(0),
                                                  _stream_ptr(stream)))
 
-    def attention_kernel_kind(self, precision: int, heads: int, head_dim: int) -> int:
-        return int(library().awa_attention_kernel_kind(self._handle, precision, heads, head_dim))
+    def attention_kernel_kind(self, precision: int, heads: int, head_dim: int, in_dtype=None) -> int:
+        """1 = tcgen05 kernel, 2 = fp32 SIMT kernel. `in_dtype` (a torch dtype) defaults to bf16 at
+        AWA_PREC_BF16 and fp32 otherwise."""
+        torch = _torch()
+        if in_dtype is None:
+            in_dtype = torch.bfloat16 if precision == AWA_PREC_BF16 else torch.float32
+        code = AWA_BF16 if in_dtype == torch.bfloat16 else AWA_F32
+        return int(library().awa_attention_kernel_kind(self._handle, precision, code, heads, head_dim))
 
 
 def device_status() -> None:

@@ -1,19 +1,37 @@
 // awa_attn_tc.cu -- bf16 window attention on the sm_100a tensor cores
-// (tcgen05.mma, fp32 accumulators in TMEM), for the bf16 DiT blocks.
+// (tcgen05.mma, fp32 accumulators in TMEM, TMA box loads), for the bf16
+// DiT blocks.
 //
 // Math of SeedVR2WindowAttention::forward (awa_layers.cpp:1062-1120): per
 // window and head, softmax(Q K^T / sqrt(d)) V over the window rows.
 //
 // Persistent, warp-specialised kernel: one CTA per SM walks a list of jobs;
-// a job is (window, head, pair of 128-row query tiles A and B). Roles:
+// a job is (window, head, pair of 128-row query tiles A and B). A window's
+// rows are handled in key blocks of 64 rows:
 //
-//   warps 8-11  producer. Q: each thread owns one query row (= one TMEM
-//               lane), loads it from HBM into registers, rotates it (3D RoPE,
-//               bf16x2 arithmetic) and writes it into TMEM with tcgen05.st --
-//               Q never touches shared memory. K: 16 threads per 256-byte row,
-//               global -> registers -> rotate -> 128-byte-swizzled shared
-//               store. V: cp.async straight into its swizzled position.
-//               K/V move through a ring of 64-key stages.
+//   fused path  (rows read straight from the source QKV): one block per
+//               (frame, box) of the window -- a box of tc_bhc x tc_bwc tokens
+//               laid over the window at its nominal (unclipped) origin, read
+//               with ONE 4-D TMA load per 64 features (features x w x h x t
+//               tensor map). The window rule clips windows only at the grid's
+//               edges, so the part of a box outside its window lies outside
+//               the grid and TMA fills it with zeros. Text rows follow in
+//               blocks of 64 (2-D loads of the text QKV).
+//   packed path (rows from a packed QKV, RoPE already applied): dense blocks
+//               of 64 consecutive packed rows (2-D loads).
+//
+// Each block costs 4 TMA instructions of up to 8 KB (K and V, two 64-feature
+// panels), few enough for one warp to keep HBM busy. Rows of a block that
+// are not window rows (box parts outside the window, the text tail, the
+// packed tail) are masked out of the softmax as keys and dropped as queries.
+//
+// Roles:
+//   warp 13     TMA: the job's Q tiles into a staging area, K/V blocks into a
+//               ring of stages (128-byte-swizzled rows, as the MMAs read them).
+//   warps 8-11  RoPE: each thread owns one query row (= one TMEM lane), reads
+//               it from the staging tile, rotates it (3D RoPE, bf16x2
+//               arithmetic) and writes it into TMEM with tcgen05.st -- the MMA
+//               reads Q from TMEM. K is rotated in place in its stage.
 //   warp 12     MMA: one lane issues S_i = Q_i K^T (A = Q from TMEM, B = K
 //               from shared memory) and O_i += P_i V (A = P from TMEM, B = V
 //               read MN-major from the same swizzled layout), ping-ponging
@@ -25,15 +43,17 @@
 //               text rows to the fp32 partials).
 //
 // TMEM (512 columns): Q_A 0-63, Q_B 64-127, S_A 128-191, S_B 192-255,
-// O_A 256-383, O_B 384-511. Keeping Q in TMEM and rotating K on its way in
-// halves the shared-memory traffic per job, which (with 128-row MMAs reading
-// their B operand from shared memory) is the resource the kernel is bound by.
-// Hand-offs are mbarriers (tcgen05.commit for MMA completion); every wait is
-// bounded and an abort flag in shared memory stops all roles if one gives up.
+// O_A 256-383, O_B 384-511. Hand-offs are mbarriers (TMA transaction counts,
+// tcgen05.commit for MMA completion); every wait is bounded and an abort flag
+// in shared memory stops all roles if one gives up. Before the CTA exits, the
+// TMA warp waits for its copies in flight and the MMA warp for its MMAs.
 #include "awa_rows.cuh"
 #include "tcgen05.cuh"
 
+#include <cuda.h>
 #include <cuda_bf16.h>
+
+#include <mutex>
 
 namespace awa
 {
@@ -42,44 +62,49 @@ namespace
 
 using bf16 = __nv_bfloat16;
 
-constexpr int kQRows = 128;                    // query rows per tile
-constexpr int kKeys = 64;                      // keys per K/V block
+constexpr int kQRows = 128;            // query rows per tile (two key blocks)
+constexpr int kKeys = 64;              // rows per key block
 constexpr int kHeadDim = 128;
-constexpr int kKvPanel = kKeys * 128;          // 64 bf16 features x 64 rows (8 KB)
-constexpr int kKvTile = 2 * kKvPanel;          // 64 x 128 bf16 (16 KB)
-constexpr int kStages = 5;                     // K/V ring depth
+constexpr int kKvPanel = kKeys * 128;  // 64 bf16 features x 64 rows (8 KB)
+constexpr int kKvTile = 2 * kKvPanel;  // 64 x 128 bf16 (16 KB)
+constexpr int kQPanel = kQRows * 128;  // 64 features x 128 rows (16 KB)
+constexpr int kQTile = 2 * kQPanel;    // 128 x 128 bf16 (32 KB)
+constexpr int kStages = 4;             // K/V ring depth
 constexpr int kSoftmaxWarps = 8;
-constexpr int kProducerWarp0 = 8;
+constexpr int kRopeWarp0 = 8;
 constexpr int kMmaWarp = 12;
-constexpr int kThreads = 13 * 32;
+constexpr int kTmaWarp = 13;
+constexpr int kThreads = 14 * 32;
 constexpr uint32_t kTmemColumns = 512;
 constexpr uint32_t kColQ = 0;    // + 64 * tile
 constexpr uint32_t kColS = 128;  // + 64 * tile
 constexpr uint32_t kColO = 256;  // + 128 * tile
-constexpr int kRopeSmemEntries = 4096;          // (cos, sin) bf16 pairs: 16 KB
+constexpr int kRopeSmemEntries = 4096;            // (cos, sin) bf16 pairs: 16 KB
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: healthy waits last microseconds
+constexpr uint64_t kDrainLimitNs = 200000000ull;  // 0.2 s for copies / MMAs in flight at exit
 
-// Source of one K/V row of a block (32 bytes, read with shared loads).
-struct RowRec
+// Tensor maps of one launch, [source][q, k, v] with 128-byte swizzle and
+// 64-feature boxes. Fused: source 0 = video QKV (features x w x h x t, box
+// 64 x tc_bwc x tc_bhc x 1), source 1 = text QKV (features x tokens, box 64 x
+// 64). Packed: source 0 = packed QKV (features x rows, box 64 x 64).
+struct TmaMaps
 {
-    const void* src;  // q segment of the row for this head (nullptr: padding row)
-    int64_t step;     // bytes between its q, k and v segments
-    short4 coords;    // RoPE coordinates (t, h, w)
-    int64_t pad;
+    CUtensorMap map[2][3];
 };
 
 struct Barriers
 {
-    uint64_t q_full, q_empty;
-    uint64_t kv_full[kStages], kv_empty[kStages];
+    uint64_t q_loaded, q_free, q_full, q_empty;
+    uint64_t kv_loaded[kStages], kv_full[kStages], kv_empty[kStages];
     uint64_t s_full[2], p_full[2], o_full[2], o_empty[2];
+    uint64_t mma_done;
 };
 
 struct TcShared
 {
+    uint8_t q[2][kQTile];             // Q staging of tiles A, B
     uint8_t kv[kStages][2][kKvTile];  // [stage][K, V]
     uint32_t rope[kRopeSmemEntries];  // the plan's bf16 (cos, sin) RoPE table
-    RowRec k_rows[kKeys];
     Barriers bar;
     uint32_t tmem_base;
     int abort;
@@ -90,12 +115,14 @@ struct Job
     WindowDesc win;
     int window;
     int head;
-    int qa;      // first query tile (rows 128*qa ..)
-    int length;  // window rows (video + text)
-    int blocks;  // 64-key blocks
-    bool has_b;  // second query tile exists
+    int qa;       // first query tile (rows 128*qa ..)
+    int blocks;   // 64-row key blocks of the window
+    int vblocks;  // fused: video blocks (the rest are text blocks)
+    int length;   // window rows (video + text)
+    bool has_b;   // second query tile exists
 };
 
+template <bool PACKED>
 __device__ __forceinline__ Job decode_job(const AttnArgs& a, int j)
 {
     Job job;
@@ -104,10 +131,114 @@ __device__ __forceinline__ Job decode_job(const AttnArgs& a, int j)
     job.window = item.x;
     job.win = a.plan.windows[item.x];
     job.length = job.win.video + a.plan.text_tokens;
+    if (PACKED)
+    {
+        job.vblocks = 0;
+        job.blocks = (job.length + kKeys - 1) / kKeys;
+    }
+    else
+    {
+        job.vblocks = job.win.nt * a.plan.tc_nhc * a.plan.tc_nwc;
+        job.blocks = job.vblocks + a.plan.tc_text_blocks;
+    }
     job.qa = 2 * item.y;
-    job.blocks = (job.length + kKeys - 1) / kKeys;
-    job.has_b = (job.qa + 1) * kQRows < job.length;
+    job.has_b = 2 * (job.qa + 1) < job.blocks;
     return job;
+}
+
+// Where key block b of the job comes from.
+struct BlockGeo
+{
+    bool video;  // fused: a video box (else text rows / packed rows)
+    int lt;      // video: window-local frame
+    int hb, wb;  // video: box start relative to the nominal window origin
+    int first;   // text: first text token; packed: first window row
+};
+
+template <bool PACKED>
+__device__ __forceinline__ BlockGeo block_geo(const AttnArgs& a, const Job& job, int b)
+{
+    BlockGeo g;
+    g.lt = g.hb = g.wb = 0;
+    if (PACKED)
+    {
+        g.video = false;
+        g.first = b * kKeys;
+        return g;
+    }
+    g.video = b < job.vblocks;
+    if (g.video)
+    {
+        const int per_frame = a.plan.tc_nhc * a.plan.tc_nwc;
+        g.lt = b / per_frame;
+        const int rem = b - g.lt * per_frame;
+        const int hc = rem / a.plan.tc_nwc;
+        g.hb = hc * a.plan.tc_bhc;
+        g.wb = (rem - hc * a.plan.tc_nwc) * a.plan.tc_bwc;
+        g.first = 0;
+    }
+    else
+        g.first = (b - job.vblocks) * kKeys;
+    return g;
+}
+
+// Walks a job's blocks in order without divisions.
+struct BlockCursor
+{
+    int b = 0, lt = 0, hc = 0, wc = 0;
+
+    template <bool PACKED>
+    __device__ __forceinline__ BlockGeo geo(const AttnArgs& a, const Job& job) const
+    {
+        BlockGeo g;
+        g.video = !PACKED && b < job.vblocks;
+        g.lt = lt;
+        g.hb = hc * a.plan.tc_bhc;
+        g.wb = wc * a.plan.tc_bwc;
+        g.first = PACKED ? b * kKeys : (b - job.vblocks) * kKeys;
+        return g;
+    }
+
+    __device__ __forceinline__ void next(const AttnArgs& a)
+    {
+        b++;
+        if (++wc == a.plan.tc_nwc)
+        {
+            wc = 0;
+            if (++hc == a.plan.tc_nhc)
+            {
+                hc = 0;
+                lt++;
+            }
+        }
+    }
+};
+
+__device__ __forceinline__ uint64_t low_bits(int n)
+{
+    return n >= 64 ? ~0ull : n <= 0 ? 0ull : (1ull << n) - 1ull;
+}
+
+// Bit i set <=> row i of block b is a window row.
+template <bool PACKED>
+__device__ __forceinline__ uint64_t block_mask(const AttnArgs& a, const Job& job, const BlockGeo& g)
+{
+    if (PACKED)
+        return low_bits(job.length - g.first);
+    if (!g.video)
+        return low_bits(a.plan.text_tokens - g.first);
+    // window part of the box: rows [h_a, h_b) x columns [w_a, w_b) of the box
+    const int hoff = job.win.h0 - job.win.h0n - g.hb;
+    const int woff = job.win.w0 - job.win.w0n - g.wb;
+    const int h_a = max(hoff, 0), h_b = min(hoff + job.win.nh, a.plan.tc_bhc);
+    const int w_a = max(woff, 0), w_b = min(woff + job.win.nw, a.plan.tc_bwc);
+    if (h_a >= h_b || w_a >= w_b)
+        return 0ull;
+    const uint64_t row = low_bits(w_b) & ~low_bits(w_a);
+    uint64_t m = 0ull;
+    for (int h = h_a; h < h_b; h++)
+        m |= row << (h * a.plan.tc_bwc);
+    return m;
 }
 
 // ---------------------------------------------------------------- waits
@@ -136,19 +267,68 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
     }
 }
 
+// Bounded wait used on the way out (ignores the abort flag).
+__device__ __forceinline__ void drain_bar(uint64_t* bar, uint32_t parity, int* error_flag, int code)
+{
+    const uint64_t start = tc::global_ns();
+    while (!tc::mbar_try_wait_sleep(bar, parity, 20000))
+        if (tc::global_ns() - start > kDrainLimitNs)
+        {
+            if (error_flag)
+                atomicCAS(error_flag, 0, code);
+            return;
+        }
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar)
 {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_addr(bar)) : "memory");
 }
 
-__device__ __forceinline__ void producer_sync()
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
 {
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::smem_addr(bar)), "r"(bytes)
+                 : "memory");
 }
 
-// Barrier over the 128 producer threads that also ANDs their flags, so a wait
-// that gave up in one thread makes every producer thread leave together.
-__device__ __forceinline__ bool producer_all(bool ok)
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(tc::smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                            uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(tc::smem_addr(bar))
+        : "memory");
+}
+
+// One panel (64 features) of block b's rows of segment m (0 q, 1 k, 2 v)
+// into shared memory at dst.
+template <bool PACKED>
+__device__ __forceinline__ void load_block_panel(const AttnArgs& a, const TmaMaps& maps, const Job& job, int b,
+                                                 int m, int panel, uint32_t dst, uint64_t* bar)
+{
+    const int x = job.head * kHeadDim + 64 * panel;
+    const BlockGeo g = block_geo<PACKED>(a, job, b);
+    if (PACKED)
+        tma_load_2d(dst, &maps.map[0][m], x, job.win.offset + g.first, bar);
+    else if (g.video)
+        tma_load_4d(dst, &maps.map[0][m], x, job.win.w0n + g.wb, job.win.h0n + g.hb, job.win.t0 + g.lt, bar);
+    else
+        tma_load_2d(dst, &maps.map[1][m], x, g.first, bar);
+}
+
+// Barrier over the 128 RoPE threads that also ANDs their flags, so a wait
+// that gave up in one thread makes every RoPE thread leave together.
+__device__ __forceinline__ bool rope_all(bool ok)
 {
     uint32_t r;
     asm volatile(
@@ -166,48 +346,6 @@ __device__ __forceinline__ bool producer_all(bool ok)
 __device__ __forceinline__ bool warp_all(bool ok)
 {
     return __all_sync(0xffffffffu, ok);
-}
-
-// ---------------------------------------------------------------- shared-memory access
-// Explicit shared-memory accesses (32-bit shared addresses), so the compiler
-// knows they cannot alias global memory and keeps them in program order.
-__device__ __forceinline__ void lds_row(uint32_t addr, uint64_t& src, uint64_t& step, uint64_t& coords)
-{
-    asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(src), "=l"(step) : "r"(addr));
-    asm volatile("ld.shared.u64 %0, [%1+16];" : "=l"(coords) : "r"(addr));
-}
-
-__device__ __forceinline__ uint32_t lds_u32(uint32_t addr)
-{
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-    return v;
-}
-
-__device__ __forceinline__ void sts_u4(uint32_t addr, uint4 v)
-{
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
-}
-
-// 16-byte asynchronous global -> shared copy; src_bytes 0 writes zeros.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes)
-{
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-
-__device__ __forceinline__ void cp_async_commit()
-{
-    asm volatile("cp.async.commit_group;" ::: "memory");
-}
-
-__device__ __forceinline__ void cp_async_wait_all()
-{
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-}
-
-__device__ __forceinline__ short4 unpack_coords(uint64_t co)
-{
-    return make_short4((short)(co & 0xffff), (short)((co >> 16) & 0xffff), (short)((co >> 32) & 0xffff), 0);
 }
 
 // ---------------------------------------------------------------- RoPE in bf16x2
@@ -230,99 +368,13 @@ __device__ __forceinline__ int rope_axis(int pair, int ppa)
     return pair >= 2 * ppa ? 2 : pair >= ppa ? 1 : 0;
 }
 
-__device__ __forceinline__ int coord_of(short4 co, int axis)
-{
-    return axis == 0 ? co.x : axis == 1 ? co.y : co.z;
-}
-
-// Per-thread constants of the RoPE pairs of its 16-byte chunk (features 8c .. 8c+7).
-struct RopeLanes
-{
-    int within[4];
-    int axis[4];
-    bool active[4];
-};
-
-__device__ __forceinline__ RopeLanes rope_lanes(const PlanDevice& plan, int c)
-{
-    RopeLanes rl;
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-    {
-        const int pair = 4 * c + i;
-        rl.active[i] = 2 * pair < plan.rope_dim;
-        rl.axis[i] = rope_axis(pair, plan.pairs_per_axis);
-        rl.within[i] = pair - rl.axis[i] * plan.pairs_per_axis;
-    }
-    return rl;
-}
-
-// ---------------------------------------------------------------- raw row loads
-template <typename T>
-struct Raw8;
-template <>
-struct Raw8<bf16>
-{
-    uint4 u;
-};
-template <>
-struct Raw8<float>
-{
-    float4 a, b;
-};
-
-__device__ __forceinline__ Raw8<bf16> load_raw(const bf16* p)
-{
-    return {__ldg(reinterpret_cast<const uint4*>(p))};
-}
-__device__ __forceinline__ Raw8<float> load_raw(const float* p)
-{
-    return {__ldg(reinterpret_cast<const float4*>(p)), __ldg(reinterpret_cast<const float4*>(p) + 1)};
-}
-__device__ __forceinline__ void zero_raw(Raw8<bf16>& r)
-{
-    r.u = make_uint4(0, 0, 0, 0);
-}
-__device__ __forceinline__ void zero_raw(Raw8<float>& r)
-{
-    r.a = r.b = make_float4(0.f, 0.f, 0.f, 0.f);
-}
-__device__ __forceinline__ uint4 to_bf16x8(const Raw8<bf16>& r)
-{
-    return r.u;
-}
-__device__ __forceinline__ uint4 to_bf16x8(const Raw8<float>& r)
-{
-    return make_uint4(pack_bf16x2(r.a.x, r.a.y), pack_bf16x2(r.a.z, r.a.w), pack_bf16x2(r.b.x, r.b.y),
-                      pack_bf16x2(r.b.z, r.b.w));
-}
-
 // Byte offset of 16-byte chunk c (0..15 along the 128 features) of row r in a
-// swizzled 64-row K/V tile: two 64-feature panels, 128-byte rows, chunk XOR row%8.
-__device__ __forceinline__ uint32_t swizzled_offset(int r, int c)
+// swizzled tile of `rows` rows: two 64-feature panels, 128-byte rows, chunk
+// XOR row%8 -- the layout the 128-byte-swizzle TMA writes from a 1024-byte
+// aligned base.
+__device__ __forceinline__ uint32_t swizzled_offset(int rows, int r, int c)
 {
-    return (uint32_t)((c >> 3) * kKvPanel + r * 128 + ((((c & 7) ^ (r & 7))) << 4));
-}
-
-template <bool PACKED, typename TIn>
-__device__ __forceinline__ void row_source(const AttnArgs& a, const Job& job, int row, const TIn*& src, int64_t& step,
-                                           short4& coords)
-{
-    if (row < job.length)
-    {
-        const RowRef ref = window_row<PACKED>(a, job.win, row, job.head);
-        const TIn* base =
-            PACKED ? static_cast<const TIn*>(a.qkv) : static_cast<const TIn*>(ref.is_text ? a.text_qkv : a.video_qkv);
-        src = base + ref.offset;
-        step = ref.qkv_step;
-        coords = ref.coords;
-    }
-    else
-    {
-        src = nullptr;
-        step = 0;
-        coords = make_short4(0, 0, 0, 0);
-    }
+    return (uint32_t)((c >> 3) * rows * 128 + r * 128 + ((((c & 7) ^ (r & 7))) << 4));
 }
 
 // ---------------------------------------------------------------- MMA helpers
@@ -351,181 +403,290 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t tmem_p, uint3
                    (accumulate || ks > 0) ? 1u : 0u);
 }
 
-__device__ __forceinline__ int block_n(const Job& job, int kb)
+// Rows the loads of block b write: a video box writes tc_rows of the 64.
+template <bool PACKED>
+__device__ __forceinline__ int box_rows(const AttnArgs& a, const Job& job, int b)
 {
-    const int valid = min(kKeys, job.length - kb * kKeys);
-    return max(16, (valid + 15) & ~15);
+    return (!PACKED && b < job.vblocks) ? a.plan.tc_rows : kKeys;
 }
 
-// ---------------------------------------------------------------- producer
-// One query row (this thread's TMEM lane) into TMEM columns tmem_q ..+63:
-// each half of the row (8 chunks) is loaded before any of it is rotated.
-template <bool ROPE, typename TIn>
-__device__ __forceinline__ void load_q_row(const AttnArgs& a, const TIn* src, short4 co, uint32_t tmem_q,
-                                           uint32_t rope_table)
+// Keys of block b that the MMAs cover (a multiple of 16): rows past them are
+// never window rows. Rows below it that are not window rows are masked; they
+// hold zeros or earlier rows of this launch (text rows: every window attends
+// to them, so they carry nothing a window's output does not already see).
+template <bool PACKED>
+__device__ __forceinline__ int block_n(const AttnArgs& a, const Job& job, int b)
 {
-    const int ppa = a.plan.pairs_per_axis;
-#pragma unroll
-    for (int h = 0; h < 2; h++)
+    int rows = box_rows<PACKED>(a, job, b);
+    if (PACKED)
+        rows = min(rows, job.length - b * kKeys);
+    else if (b >= job.vblocks)
+        rows = min(rows, a.plan.text_tokens - (b - job.vblocks) * kKeys);
+    return max(16, (rows + 15) & ~15);
+}
+
+// ---------------------------------------------------------------- TMA warp
+template <bool PACKED>
+__device__ void tma_role(const AttnArgs& a, const TmaMaps& maps, TcShared& sh, int njobs)
+{
+    const int lane = threadIdx.x & 31;
+    volatile int* abort = &sh.abort;
+    uint32_t q_free_phase = 1;  // a fresh barrier reads as "released"
+    uint32_t q_issued = 0;      // Q loads issued so far
+    uint32_t g = 0;             // K/V blocks issued so far
+    bool ok = true;
+    for (int j = blockIdx.x; j < njobs && ok; j += gridDim.x)
     {
-        Raw8<TIn> raw[8];
-#pragma unroll
-        for (int k = 0; k < 8; k++)
+        const Job job = decode_job<PACKED>(a, j);
+        // ---- the job's Q tiles (up to 4 blocks) into the staging area
+        if (!warp_all(wait_bar(&sh.bar.q_free, q_free_phase, abort, a.error_flag, 41)))
+            break;
+        q_free_phase ^= 1;
+        const int qb0 = 2 * job.qa;
+        const int qblocks = min(4, job.blocks - qb0);
+        if (lane == 0)
         {
-            if (src)
-                raw[k] = load_raw(src + 8 * (8 * h + k));
-            else
-                zero_raw(raw[k]);
+            uint32_t bytes = 0;
+            for (int qb = 0; qb < qblocks; qb++)
+                bytes += 2u * 128u * (uint32_t)box_rows<PACKED>(a, job, qb0 + qb);
+            mbar_arrive_expect_tx(&sh.bar.q_loaded, bytes);
         }
-        uint32_t words[32];
-#pragma unroll
-        for (int k = 0; k < 8; k++)
+        __syncwarp();
+        if (lane < 2 * qblocks)
         {
-            const uint4 w = to_bf16x8(raw[k]);
-            words[4 * k + 0] = w.x;
-            words[4 * k + 1] = w.y;
-            words[4 * k + 2] = w.z;
-            words[4 * k + 3] = w.w;
+            const int qb = lane >> 1, panel = lane & 1;  // block qb0 + qb -> tile qb/2, rows 64*(qb%2)
+            const uint32_t dst = tc::smem_addr(sh.q[qb >> 1]) + (uint32_t)(panel * kQPanel + (qb & 1) * kKeys * 128);
+            load_block_panel<PACKED>(a, maps, job, qb0 + qb, 0, panel, dst, &sh.bar.q_loaded);
         }
-        if (ROPE && src)
+        q_issued++;
+        // ---- K/V blocks through the ring: lanes 0-3 = (K, V) x panel
+        for (int kb = 0; kb < job.blocks; kb++)
         {
-#pragma unroll
-            for (int k = 0; k < 32; k++)
+            const int stage = g % kStages;
+            const uint32_t use = g / kStages;
+            if (!warp_all(wait_bar(&sh.bar.kv_empty[stage], (use & 1) ^ 1, abort, a.error_flag, 42)))
             {
-                const int pair = 32 * h + k;  // features 2 pair, 2 pair + 1
-                if (2 * pair < a.plan.rope_dim)
-                {
-                    const int axis = rope_axis(pair, ppa);
-                    const int idx = coord_of(co, axis) * ppa + pair - axis * ppa;
-                    words[k] = rotate_bf16x2(words[k], lds_u32(rope_table + 4u * (uint32_t)idx));
-                }
+                ok = false;
+                break;
             }
+            if (lane == 0)
+                mbar_arrive_expect_tx(&sh.bar.kv_loaded[stage], 4u * 128u * (uint32_t)box_rows<PACKED>(a, job, kb));
+            __syncwarp();
+            if (lane < 4)
+            {
+                const int kv = lane >> 1, panel = lane & 1;
+                const uint32_t dst = tc::smem_addr(sh.kv[stage][kv]) + (uint32_t)(panel * kKvPanel);
+                load_block_panel<PACKED>(a, maps, job, kb, 1 + kv, panel, dst, &sh.bar.kv_loaded[stage]);
+            }
+            g++;
         }
-        tc::tmem_st32(tmem_q + (uint32_t)(32 * h), words);
+    }
+    // Wait for the copies still in flight (only the last use of each barrier
+    // can be outstanding: the next one is issued after the previous was consumed).
+    if (q_issued > 0)
+        drain_bar(&sh.bar.q_loaded, (q_issued - 1) & 1, a.error_flag, 43);
+    for (uint32_t k = 0; k < (uint32_t)kStages && k < g; k++)
+    {
+        const uint32_t last = g - 1 - k;  // the last block issued on stage last % kStages
+        drain_bar(&sh.bar.kv_loaded[last % kStages], (last / kStages) & 1, a.error_flag, 44);
     }
 }
 
-template <bool PACKED, typename TIn>
-__device__ void producer_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t tmem)
+// ---------------------------------------------------------------- RoPE warps
+// Shared-memory round trips are slow while the tensor core and TMA stream
+// through shared memory, so every step below first issues all of its loads
+// (data and RoPE table entries) and only then computes: one round trip per
+// batch instead of a dependent chain per row.
+template <bool PACKED>
+__device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t tmem)
 {
-    const int ptid = threadIdx.x - kProducerWarp0 * 32;  // = this thread's TMEM lane
+    const int ptid = threadIdx.x - kRopeWarp0 * 32;  // = this thread's TMEM lane / Q row
     const uint32_t lane_base = (uint32_t)(ptid & ~31) << 16;
-    const int c = ptid & 15;   // K/V chunk of this thread
-    const int r0 = ptid >> 4;  // K/V rows r0 + 8 j
-    const RopeLanes rl = rope_lanes(a.plan, c);
+    const int c = ptid & 15;    // K chunk of this thread
+    const int kr0 = ptid >> 4;  // K rows kr0 + 8 jj
     const int ppa = a.plan.pairs_per_axis;
-    const uint32_t rope_table = tc::smem_addr(sh.rope);
-    const uint32_t k_rows = tc::smem_addr(sh.k_rows);
+    const int rope_dim = a.plan.rope_dim;
+    const int bwc = a.plan.tc_bwc > 0 ? a.plan.tc_bwc : 1;
+    const uint32_t* table = sh.rope;
     volatile int* abort = &sh.abort;
-    uint32_t q_empty_phase = 1;  // a fresh barrier reads as "released"
-    uint32_t g = 0;              // K/V blocks produced so far
+    uint32_t q_loaded_phase = 0;
+    uint32_t q_empty_phase = 1;  // TMEM Q starts free
+    uint32_t g = 0;
+    // per-thread constants of the K chunk: pairs 4c .. 4c+3
+    int k_axis[4], k_within[4];
+    bool k_active[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+    {
+        const int pair = 4 * c + i;
+        k_active[i] = 2 * pair < rope_dim;
+        k_axis[i] = rope_axis(pair, ppa);
+        k_within[i] = pair - k_axis[i] * ppa;
+    }
+    // (h, w) within a box of this thread's K rows kr0 + 8 jj and of its Q row
+    int k_hw[8];
+#pragma unroll
+    for (int jj = 0; jj < 8; jj++)
+        k_hw[jj] = ((kr0 + 8 * jj) / bwc) * 256 + (kr0 + 8 * jj) % bwc;
+    const int q_h = (ptid & 63) / bwc, q_w = (ptid & 63) % bwc;
+
     for (int j = blockIdx.x; j < njobs; j += gridDim.x)
     {
-        const Job job = decode_job(a, j);
-        // ---- Q rows into TMEM (once the previous job's S MMAs are done with it)
-        if (!producer_all(wait_bar(&sh.bar.q_empty, q_empty_phase, abort, a.error_flag, 11)))
+        const Job job = decode_job<PACKED>(a, j);
+        const int hoff = job.win.h0 - job.win.h0n, woff = job.win.w0 - job.win.w0n;
+        // ---- Q: staging -> (rotate) -> TMEM
+        if (!rope_all(wait_bar(&sh.bar.q_loaded, q_loaded_phase, abort, a.error_flag, 11)))
+            return;
+        q_loaded_phase ^= 1;
+        if (!rope_all(wait_bar(&sh.bar.q_empty, q_empty_phase, abort, a.error_flag, 12)))
             return;
         q_empty_phase ^= 1;
         tc::fence_after_sync();
-#pragma unroll
+#pragma unroll 1
         for (int t = 0; t < 2; t++)
         {
             if (t == 1 && !job.has_b)
                 break;
-            const TIn* src;
-            int64_t step;
-            short4 co;
-            row_source<PACKED, TIn>(a, job, (job.qa + t) * kQRows + ptid, src, step, co);
-            load_q_row<!PACKED, TIn>(a, src, co, tmem + lane_base + kColQ + 64u * t, rope_table);
+            const uint8_t* tile = sh.q[t];
+            // table entry of pair p on axis x: base[x] + p (base[x] = (coord_x - x) * ppa)
+            int base[3] = {0, 0, 0};
+            bool rotate = false;
+            if (!PACKED)
+            {
+                const int b = 2 * (job.qa + t) + (ptid >> 6);
+                if (b < job.blocks)
+                {
+                    const BlockGeo geo = block_geo<PACKED>(a, job, b);
+                    if ((block_mask<PACKED>(a, job, geo) >> (ptid & 63)) & 1ull)
+                    {
+                        int ct, ch, cw;
+                        if (geo.video)
+                        {
+                            ct = a.plan.text_tokens + geo.lt;
+                            ch = geo.hb + q_h - hoff;
+                            cw = geo.wb + q_w - woff;
+                        }
+                        else
+                            ct = ch = cw = geo.first + (ptid & 63);
+                        base[0] = ct * ppa;
+                        base[1] = (ch - 1) * ppa;
+                        base[2] = (cw - 2) * ppa;
+                        rotate = true;
+                    }
+                }
+            }
+            // half a row (8 chunks = 32 bf16 pairs = 32 TMEM columns) per batch
+#pragma unroll 1
+            for (int h = 0; h < 2; h++)
+            {
+                uint32_t words[32];
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                {
+                    const uint4 w = *reinterpret_cast<const uint4*>(tile + swizzled_offset(kQRows, ptid, 8 * h + k));
+                    words[4 * k + 0] = w.x;
+                    words[4 * k + 1] = w.y;
+                    words[4 * k + 2] = w.z;
+                    words[4 * k + 3] = w.w;
+                }
+                if (!PACKED && rotate)
+                {
+                    uint32_t cs[32];
+#pragma unroll
+                    for (int k = 0; k < 32; k++)
+                    {
+                        const int pair = 32 * h + k;  // features 2 pair, 2 pair + 1
+                        const int b = pair < ppa ? base[0] : pair < 2 * ppa ? base[1] : base[2];
+                        cs[k] = 2 * pair < rope_dim ? table[b + pair] : 0u;
+                    }
+#pragma unroll
+                    for (int k = 0; k < 32; k++)
+                        if (2 * (32 * h + k) < rope_dim)
+                            words[k] = rotate_bf16x2(words[k], cs[k]);
+                }
+                tc::tmem_st32(tmem + lane_base + kColQ + 64u * t + 32u * h, words);
+            }
         }
         tc::tmem_wait_st();
         tc::fence_before_sync();
         mbar_arrive(&sh.bar.q_full);
-        // ---- K/V blocks through the ring
-        for (int kb = 0; kb < job.blocks; kb++, g++)
+        mbar_arrive(&sh.bar.q_free);
+        // ---- K blocks: rotate in place (fused); zero the V rows past the
+        // window's end (packed: they belong to the next window); hand the
+        // stage to the MMA
+        BlockCursor cur;
+        for (int kb = 0; kb < job.blocks; kb++, g++, cur.next(a))
         {
             const int stage = g % kStages;
             const uint32_t use = g / kStages;
-            // also orders every producer thread after its reads of the previous row records
-            if (!producer_all(wait_bar(&sh.bar.kv_empty[stage], (use & 1) ^ 1, abort, a.error_flag, 12)))
+            const BlockGeo geo = cur.geo<PACKED>(a, job);
+            const uint64_t mask = block_mask<PACKED>(a, job, geo);
+            if (!rope_all(wait_bar(&sh.bar.kv_loaded[stage], use & 1, abort, a.error_flag, 13)))
                 return;
-            if (ptid < kKeys)
+            if (!PACKED)
             {
-                const TIn* src;
-                int64_t step;
-                short4 co;
-                row_source<PACKED, TIn>(a, job, kb * kKeys + ptid, src, step, co);
-                RowRec& rec = sh.k_rows[ptid];
-                rec.src = src;
-                rec.step = step * (int64_t)sizeof(TIn);
-                rec.coords = co;
-            }
-            producer_sync();
-            const uint32_t k_tile = tc::smem_addr(sh.kv[stage][0]);
-            const uint32_t v_tile = tc::smem_addr(sh.kv[stage][1]);
-            uint64_t src[8], step[8], cow[8];
+                uint8_t* k_tile = sh.kv[stage][0];
+                uint4 data[8];
 #pragma unroll
-            for (int jj = 0; jj < 8; jj++)
-                lds_row(k_rows + (uint32_t)(r0 + 8 * jj) * (uint32_t)sizeof(RowRec), src[jj], step[jj], cow[jj]);
-            // V: asynchronous copies (bf16) ...
-            if (sizeof(TIn) == 2)
-            {
+                for (int jj = 0; jj < 8; jj++)
+                    data[jj] = *reinterpret_cast<const uint4*>(k_tile + swizzled_offset(kKeys, kr0 + 8 * jj, c));
+                uint32_t cs[8][4];
 #pragma unroll
                 for (int jj = 0; jj < 8; jj++)
                 {
-                    const char* p = src[jj] ? reinterpret_cast<const char*>(src[jj] + 2 * step[jj]) + 16 * c
-                                            : reinterpret_cast<const char*>(a.plan.windows);
-                    cp_async16(v_tile + swizzled_offset(r0 + 8 * jj, c), p, src[jj] ? 16u : 0u);
-                }
-                cp_async_commit();
-            }
-            // ... while K goes through registers and is rotated on the way
-            // (fp32 input: V takes this path too, converted to bf16).
-#pragma unroll
-            for (int kv = 0; kv < (sizeof(TIn) == 2 ? 1 : 2); kv++)
-            {
-                Raw8<TIn> raw[8];
-#pragma unroll
-                for (int jj = 0; jj < 8; jj++)
-                {
-                    if (src[jj])
-                        raw[jj] = load_raw(
-                            reinterpret_cast<const TIn*>(src[jj] + (uint64_t)(1 + kv) * step[jj]) + 8 * c);
-                    else
-                        zero_raw(raw[jj]);
-                }
-#pragma unroll
-                for (int jj = 0; jj < 8; jj++)
-                {
-                    uint4 w = to_bf16x8(raw[jj]);
-                    if (!PACKED && kv == 0 && src[jj])
+                    const int r = kr0 + 8 * jj;
+                    const bool valid = (mask >> r) & 1ull;
+                    int co[3];
+                    if (geo.video)
                     {
-                        const short4 co = unpack_coords(cow[jj]);
-                        uint32_t t[4];
-#pragma unroll
-                        for (int i = 0; i < 4; i++)
-                            if (rl.active[i])
-                                t[i] = lds_u32(rope_table +
-                                               4u * (uint32_t)(coord_of(co, rl.axis[i]) * ppa + rl.within[i]));
-                        uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                        for (int i = 0; i < 4; i++)
-                            if (rl.active[i])
-                                words[i] = rotate_bf16x2(words[i], t[i]);
-                        w = make_uint4(words[0], words[1], words[2], words[3]);
+                        co[0] = a.plan.text_tokens + geo.lt;
+                        co[1] = geo.hb + (k_hw[jj] >> 8) - hoff;
+                        co[2] = geo.wb + (k_hw[jj] & 255) - woff;
                     }
-                    sts_u4((kv == 0 ? k_tile : v_tile) + swizzled_offset(r0 + 8 * jj, c), w);
+                    else
+                        co[0] = co[1] = co[2] = geo.first + r;
+#pragma unroll
+                    for (int i = 0; i < 4; i++)
+                    {
+                        const int axis = k_axis[i];
+                        const int coord = axis == 0 ? co[0] : axis == 1 ? co[1] : co[2];
+                        // rows outside the window are masked keys: any in-range entry will do
+                        cs[jj][i] = table[valid && k_active[i] ? coord * ppa + k_within[i] : 0];
+                    }
                 }
+#pragma unroll
+                for (int jj = 0; jj < 8; jj++)
+                {
+                    uint32_t words[4] = {data[jj].x, data[jj].y, data[jj].z, data[jj].w};
+#pragma unroll
+                    for (int i = 0; i < 4; i++)
+                        if (k_active[i])
+                            words[i] = rotate_bf16x2(words[i], cs[jj][i]);
+                    *reinterpret_cast<uint4*>(k_tile + swizzled_offset(kKeys, kr0 + 8 * jj, c)) =
+                        make_uint4(words[0], words[1], words[2], words[3]);
+                }
+                // generic-proxy writes -> visible to the tensor core's async-proxy reads
+                tc::fence_async_smem();
             }
-            if (sizeof(TIn) == 2)
-                cp_async_wait_all();
-            tc::fence_async_smem();
+            else if (mask != ~0ull)
+            {
+                uint8_t* v_tile = sh.kv[stage][1];
+#pragma unroll
+                for (int jj = 0; jj < 8; jj++)
+                {
+                    const int r = kr0 + 8 * jj;
+                    if (!((mask >> r) & 1ull))
+                        *reinterpret_cast<uint4*>(v_tile + swizzled_offset(kKeys, r, c)) = make_uint4(0, 0, 0, 0);
+                }
+                tc::fence_async_smem();
+            }
             mbar_arrive(&sh.bar.kv_full[stage]);
         }
     }
 }
 
 // ---------------------------------------------------------------- MMA issuer
+template <bool PACKED>
 __device__ void mma_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t tmem)
 {
     const bool leader = (threadIdx.x & 31) == 0;
@@ -537,15 +698,16 @@ __device__ void mma_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t tm
     const uint32_t tmem_q[2] = {tmem + kColQ, tmem + kColQ + 64};
     const uint32_t tmem_s[2] = {tmem + kColS, tmem + kColS + 64};
     const uint32_t tmem_o[2] = {tmem + kColO, tmem + kColO + 128};
-    for (int j = blockIdx.x; j < njobs; j += gridDim.x)
+    bool ok = true;
+    for (int j = blockIdx.x; j < njobs && ok; j += gridDim.x)
     {
-        const Job job = decode_job(a, j);
+        const Job job = decode_job<PACKED>(a, j);
         const int slots = job.has_b ? 2 : 1;
         if (!warp_all(wait_bar(&sh.bar.q_full, q_full_phase, abort, a.error_flag, 21)))
-            return;
+            break;
         q_full_phase ^= 1;
         if (!warp_all(wait_bar(&sh.bar.kv_full[g % kStages], (g / kStages) & 1, abort, a.error_flag, 22)))
-            return;
+            break;
         tc::fence_after_sync();
         if (leader)
         {
@@ -554,17 +716,17 @@ __device__ void mma_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t tm
             for (int s = 0; s < 2; s++)
                 if (s < slots)
                 {
-                    issue_qk(tmem_s[s], tmem_q[s], k_addr, block_n(job, 0));
+                    issue_qk(tmem_s[s], tmem_q[s], k_addr, block_n<PACKED>(a, job, 0));
                     tc::mma_commit(&sh.bar.s_full[s]);
                 }
             if (job.blocks == 1)
                 tc::mma_commit(&sh.bar.q_empty);
         }
         __syncwarp();
-        for (int kb = 0; kb < job.blocks; kb++)
+        for (int kb = 0; kb < job.blocks && ok; kb++)
         {
             const uint32_t gk = g + kb;
-            const int n = block_n(job, kb);
+            const int n = block_n<PACKED>(a, job, kb);
             const uint32_t v_addr = tc::smem_addr(sh.kv[gk % kStages][1]);
             const bool more = kb + 1 < job.blocks;
 #pragma unroll
@@ -573,18 +735,27 @@ __device__ void mma_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t tm
                 if (s >= slots)
                     break;
                 if (!warp_all(wait_bar(&sh.bar.p_full[s], p_phase[s], abort, a.error_flag, 23)))
-                    return;
+                {
+                    ok = false;
+                    break;
+                }
                 p_phase[s] ^= 1;
                 if (kb == 0)
                 {
                     if (!warp_all(wait_bar(&sh.bar.o_empty[s], o_empty_phase[s], abort, a.error_flag, 24)))
-                        return;
+                    {
+                        ok = false;
+                        break;
+                    }
                     o_empty_phase[s] ^= 1;
                 }
                 if (more && s == 0 &&
                     !warp_all(wait_bar(&sh.bar.kv_full[(gk + 1) % kStages], ((gk + 1) / kStages) & 1, abort,
                                        a.error_flag, 25)))
-                    return;
+                {
+                    ok = false;
+                    break;
+                }
                 tc::fence_after_sync();
                 if (leader)
                 {
@@ -595,12 +766,14 @@ __device__ void mma_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t tm
                         // S of the next block overwrites P of this one: tcgen05.mma
                         // operations of one thread execute in issue order.
                         issue_qk(tmem_s[s], tmem_q[s], tc::smem_addr(sh.kv[(gk + 1) % kStages][0]),
-                                 block_n(job, kb + 1));
+                                 block_n<PACKED>(a, job, kb + 1));
                         tc::mma_commit(&sh.bar.s_full[s]);
                     }
                 }
                 __syncwarp();
             }
+            if (!ok)
+                break;
             if (leader)
             {
                 if (kb + 2 == job.blocks)
@@ -611,6 +784,11 @@ __device__ void mma_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t tm
         }
         g += job.blocks;
     }
+    // every MMA this thread issued is complete before TMEM is released
+    if (leader)
+        tc::mma_commit(&sh.bar.mma_done);
+    __syncwarp();
+    drain_bar(&sh.bar.mma_done, 0, a.error_flag, 26);
 }
 
 // ---------------------------------------------------------------- softmax + epilogue
@@ -630,32 +808,44 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
     uint32_t pv_count = 0;  // PV MMAs of this slot issued so far (o_full completions)
     for (int j = blockIdx.x; j < njobs; j += gridDim.x)
     {
-        const Job job = decode_job(a, j);
+        const Job job = decode_job<PACKED>(a, j);
         if (slot == 1 && !job.has_b)
             continue;
-        const int row = (job.qa + slot) * kQRows + r;
+        // this thread's query row: row i of block qb
+        const int qb = 2 * (job.qa + slot) + (r >> 6);
+        const int qi = r & 63;
         int64_t dst = -1;
         bool text_row = false;
-        if (row < job.length)
+        if (qb < job.blocks)
         {
-            if (PACKED)
-                dst = (int64_t)(job.win.offset + row) * a.out_token_stride + (int64_t)job.head * kHeadDim;
-            else if (row < job.win.video)
-                dst = window_row<false>(a, job.win, row, job.head).token * a.out_token_stride +
-                      (int64_t)job.head * kHeadDim;
-            else
+            const BlockGeo geo = block_geo<PACKED>(a, job, qb);
+            if ((block_mask<PACKED>(a, job, geo) >> qi) & 1ull)
             {
-                text_row = true;
-                dst = ((int64_t)(job.window - a.window_begin) * text + (row - job.win.video)) * a.heads * kHeadDim +
-                      (int64_t)job.head * kHeadDim;
+                if (PACKED)
+                    dst = (int64_t)(job.win.offset + geo.first + qi) * a.out_token_stride +
+                          (int64_t)job.head * kHeadDim;
+                else if (geo.video)
+                {
+                    const int h = job.win.h0n + geo.hb + qi / a.plan.tc_bwc;
+                    const int w = job.win.w0n + geo.wb + qi % a.plan.tc_bwc;
+                    const int64_t token =
+                        ((int64_t)(job.win.t0 + geo.lt) * a.plan.source_h + h) * a.plan.source_w + w;
+                    dst = token * a.out_token_stride + (int64_t)job.head * kHeadDim;
+                }
+                else
+                {
+                    text_row = true;
+                    dst = ((int64_t)(job.window - a.window_begin) * text + (geo.first + qi)) * a.heads * kHeadDim +
+                          (int64_t)job.head * kHeadDim;
+                }
             }
         }
-        float m_run = 0.f;  // running max, in log2 units of the scaled scores
+        float m_run = -INFINITY;  // running max, in log2 units of the scaled scores
         float l_run = 0.f;
-        for (int kb = 0; kb < job.blocks; kb++)
+        BlockCursor cur;
+        for (int kb = 0; kb < job.blocks; kb++, cur.next(a))
         {
-            const int valid = min(kKeys, job.length - kb * kKeys);
-            const bool full = valid == kKeys;
+            const uint64_t mask = block_mask<PACKED>(a, job, cur.geo<PACKED>(a, job));
             if (!warp_all(wait_bar(&sh.bar.s_full[slot], s_phase, abort, a.error_flag, 31)))
                 return;
             s_phase ^= 1;
@@ -664,13 +854,20 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
             tc::tmem_ld32(t_s, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
             tc::tmem_ld32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
             tc::tmem_wait_ld();
+            if (mask != ~0ull)
+            {
+#pragma unroll
+                for (int i = 0; i < 64; i++)
+                    if (!((mask >> i) & 1ull))
+                        v[i] = 0xff800000u;  // -inf: p = 0
+            }
             float mxp[8];
 #pragma unroll
             for (int i = 0; i < 8; i++)
                 mxp[i] = -INFINITY;
 #pragma unroll
             for (int i = 0; i < 64; i++)
-                mxp[i & 7] = fmaxf(mxp[i & 7], (full || i < valid) ? __uint_as_float(v[i]) : -INFINITY);
+                mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(v[i]));
             const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
                                    fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
             const float m_blk = mx * scale_log2;
@@ -680,7 +877,7 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
                 m_run = m_blk;
             else if (m_blk > m_run + 8.f)
             {
-                alpha = fast_exp2(m_run - m_blk);
+                alpha = fast_exp2(m_run - m_blk);  // 0 while no key has been seen (m_run = -inf)
                 m_run = m_blk;
                 rescale = true;
             }
@@ -690,20 +887,22 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
                 if (!warp_all(wait_bar(&sh.bar.o_full[slot], (pv_count - 1) & 1, abort, a.error_flag, 32)))
                     return;
                 tc::fence_after_sync();
-#pragma unroll
-                for (int cc = 0; cc < 4; cc++)
+                // 16 columns at a time: the 64 scores stay in registers meanwhile
+#pragma unroll 1
+                for (int cc = 0; cc < 8; cc++)
                 {
-                    uint32_t o[32];
-                    tc::tmem_ld32(t_o + cc * 32, o);
+                    uint32_t o[16];
+                    tc::tmem_ld16(t_o + cc * 16, o);
                     tc::tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; i++)
+                    for (int i = 0; i < 16; i++)
                         o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tc::tmem_st32(t_o + cc * 32, o);
+                    tc::tmem_st16(t_o + cc * 16, o);
                 }
             }
             // P = exp2(s * scale - max), rounded to bf16, two keys per column, over S.
-            const float neg_m = -m_run;
+            // (No key seen yet: m_run = -inf and every p is 0.)
+            const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
             float sums[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int h = 0; h < 2; h++)
@@ -713,10 +912,8 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
                 for (int i = 0; i < 16; i++)
                 {
                     const int k = 32 * h + 2 * i;
-                    const float p0 =
-                        (full || k < valid) ? fast_exp2(fmaf(__uint_as_float(v[k]), scale_log2, neg_m)) : 0.f;
-                    const float p1 =
-                        (full || k + 1 < valid) ? fast_exp2(fmaf(__uint_as_float(v[k + 1]), scale_log2, neg_m)) : 0.f;
+                    const float p0 = fast_exp2(fmaf(__uint_as_float(v[k]), scale_log2, neg_m));
+                    const float p1 = fast_exp2(fmaf(__uint_as_float(v[k + 1]), scale_log2, neg_m));
                     sums[i & 3] += p0 + p1;
                     pk[i] = pack_bf16x2(p0, p1);
                 }
@@ -776,8 +973,9 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
     }
 }
 
-template <bool PACKED, typename TIn, typename TOut>
-__global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const AttnArgs a)
+template <bool PACKED, typename TOut>
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_tc_kernel(const AttnArgs a, const __grid_constant__ TmaMaps maps)
 {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the 128-byte swizzle atoms.
@@ -794,10 +992,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const AttnArg
     if (threadIdx.x == 0)
     {
         Barriers& b = sh.bar;
+        tc::mbar_init(&b.q_loaded, 1);
+        tc::mbar_init(&b.q_free, 128);
         tc::mbar_init(&b.q_full, 128);
         tc::mbar_init(&b.q_empty, 1);
         for (int s = 0; s < kStages; s++)
         {
+            tc::mbar_init(&b.kv_loaded[s], 1);
             tc::mbar_init(&b.kv_full[s], 128);
             tc::mbar_init(&b.kv_empty[s], 1);
         }
@@ -808,13 +1009,32 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const AttnArg
             tc::mbar_init(&b.o_full[s], 1);
             tc::mbar_init(&b.o_empty[s], 128);
         }
+        tc::mbar_init(&b.mma_done, 1);
         tc::mbar_fence_init();
         sh.abort = 0;
     }
-    // The RoPE table lives in shared memory (launch_attention_tc checks its size).
-    const int rope_entries = a.plan.max_coord * a.plan.pairs_per_axis;
-    for (int i = threadIdx.x; i < rope_entries; i += kThreads)
-        sh.rope[i] = a.plan.rope_table_bf16[i];
+    if (warp == kTmaWarp && (threadIdx.x & 31) == 0)
+    {
+        for (int s = 0; s < 2; s++)
+            for (int m = 0; m < 3; m++)
+                asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.map[s][m]))
+                             : "memory");
+    }
+    // Start from zeros: rows that no load of this launch writes stay zero.
+    {
+        uint4* z = reinterpret_cast<uint4*>(&sh.q[0][0]);
+        const int n = (int)((sizeof(sh.q) + sizeof(sh.kv)) / sizeof(uint4));
+        for (int i = threadIdx.x; i < n; i += kThreads)
+            z[i] = make_uint4(0, 0, 0, 0);
+    }
+    if (!PACKED)
+    {
+        // The RoPE table lives in shared memory (launch_attention_tc checks its size).
+        const int rope_entries = a.plan.max_coord * a.plan.pairs_per_axis;
+        for (int i = threadIdx.x; i < rope_entries; i += kThreads)
+            sh.rope[i] = a.plan.rope_table_bf16[i];
+    }
+    tc::fence_async_smem();  // the zeros land before any TMA write or MMA read
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -823,9 +1043,11 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const AttnArg
     if (warp < kSoftmaxWarps)
         softmax_role<PACKED, TOut>(a, sh, njobs, tmem);
     else if (warp < kMmaWarp)
-        producer_role<PACKED, TIn>(a, sh, njobs, tmem);
+        rope_role<PACKED>(a, sh, njobs, tmem);
+    else if (warp == kMmaWarp)
+        mma_role<PACKED>(a, sh, njobs, tmem);
     else
-        mma_role(a, sh, njobs, tmem);
+        tma_role<PACKED>(a, maps, sh, njobs);
 
     tc::fence_before_sync();
     __syncthreads();
@@ -850,43 +1072,120 @@ int sm_count()
     return count;
 }
 
-template <bool PACKED, typename TIn, typename TOut>
-int launch_tc(const AttnArgs& a, cudaStream_t stream)
+// ---------------------------------------------------------------- tensor maps (host)
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult status;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &status) == cudaSuccess &&
+            status == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// bf16 tensor map of `rank` dims (dim 0 = features, contiguous), strides in
+// bytes for dims 1.., box dims, 128-byte swizzle, zero fill outside.
+bool encode(CUtensorMap* map, const void* base, int rank, const int64_t* dims, const int64_t* strides,
+            const int* box)
+{
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15))
+        return false;
+    cuuint64_t d[4], s[3];
+    cuuint32_t b[4], e[4];
+    for (int i = 0; i < rank; i++)
+    {
+        if (dims[i] <= 0 || box[i] <= 0 || box[i] > 256)
+            return false;
+        d[i] = (cuuint64_t)dims[i];
+        b[i] = (cuuint32_t)box[i];
+        e[i] = 1;
+        if (i > 0)
+        {
+            if (strides[i - 1] % 16 || strides[i - 1] <= 0)
+                return false;
+            s[i - 1] = (cuuint64_t)strides[i - 1];
+        }
+    }
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), d, s, b, e,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool build_maps(const AttnArgs& a, int packed, TmaMaps& maps)
+{
+    const PlanDevice& p = a.plan;
+    const int64_t row = (int64_t)a.heads * a.head_dim;
+    for (int m = 0; m < 3; m++)
+    {
+        if (packed)
+        {
+            const char* base = static_cast<const char*>(a.qkv) + (int64_t)m * row * 2;
+            const int64_t dims[2] = {row, p.sequence_tokens};
+            const int64_t strides[1] = {a.qkv_token_stride * 2};
+            const int box[2] = {64, kKeys};
+            if (!encode(&maps.map[0][m], base, 2, dims, strides, box))
+                return false;
+            maps.map[1][m] = maps.map[0][m];
+            continue;
+        }
+        const char* vbase = static_cast<const char*>(a.video_qkv) + (int64_t)m * a.video_qkv_stride * 2;
+        const int64_t t_stride = a.video_token_stride * 2;
+        const int64_t vdims[4] = {row, p.source_w, p.source_h, p.source_t};
+        const int64_t vstrides[3] = {t_stride, t_stride * p.source_w, t_stride * p.source_w * p.source_h};
+        const int vbox[4] = {64, p.tc_bwc, p.tc_bhc, 1};
+        if (!encode(&maps.map[0][m], vbase, 4, vdims, vstrides, vbox))
+            return false;
+        const char* tbase = static_cast<const char*>(a.text_qkv) + (int64_t)m * a.text_qkv_stride * 2;
+        const int64_t tdims[2] = {row, p.text_tokens};
+        const int64_t tstrides[1] = {a.text_token_stride * 2};
+        const int tbox[2] = {64, kKeys};
+        if (!encode(&maps.map[1][m], tbase, 2, tdims, tstrides, tbox))
+            return false;
+    }
+    return true;
+}
+
+template <bool PACKED, typename TOut>
+int launch_tc(const AttnArgs& a, const TmaMaps& maps, cudaStream_t stream)
 {
     const size_t smem = sizeof(TcShared) + 1024;
-    auto kernel = attention_tc_kernel<PACKED, TIn, TOut>;
+    auto kernel = attention_tc_kernel<PACKED, TOut>;
     cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess)
         return (int)err;
     const long long jobs = (long long)a.item_count * a.heads;
     const int grid = (int)(jobs < sm_count() ? jobs : sm_count());
-    kernel<<<grid, kThreads, smem, stream>>>(a);
+    kernel<<<grid, kThreads, smem, stream>>>(a, maps);
     return (int)cudaGetLastError();
-}
-
-template <typename TIn, typename TOut>
-int launch_typed(const AttnArgs& a, int packed, cudaStream_t stream)
-{
-    return packed ? launch_tc<true, TIn, TOut>(a, stream) : launch_tc<false, TIn, TOut>(a, stream);
 }
 
 }  // namespace
 
 int launch_attention_tc(const AttnArgs& args, int packed, int in_dtype, int out_dtype, cudaStream_t stream)
 {
-    if (args.head_dim != kHeadDim)
+    const PlanDevice& p = args.plan;
+    if (args.head_dim != kHeadDim || in_dtype != kBF16)
         return (int)cudaErrorInvalidValue;
     if ((long long)args.item_count * args.heads > 0x7fffffffLL ||
-        (long long)args.plan.max_coord * args.plan.pairs_per_axis > kRopeSmemEntries)
+        (long long)p.max_coord * p.pairs_per_axis > kRopeSmemEntries || p.tc_rows <= 0 || p.tc_rows > kKeys ||
+        p.text_tokens <= 0)
+        return (int)cudaErrorInvalidValue;
+    TmaMaps maps;
+    if (!build_maps(args, packed, maps))
         return (int)cudaErrorInvalidValue;
     ProfileScope prof(packed ? "awa_attention_tc_packed" : "awa_attention_tc_fused", stream);
-    if (in_dtype == kF32 && out_dtype == kF32)
-        return launch_typed<float, float>(args, packed, stream);
-    if (in_dtype == kF32 && out_dtype == kBF16)
-        return launch_typed<float, bf16>(args, packed, stream);
-    if (in_dtype == kBF16 && out_dtype == kF32)
-        return launch_typed<bf16, float>(args, packed, stream);
-    return launch_typed<bf16, bf16>(args, packed, stream);
+    if (out_dtype == kF32)
+        return packed ? launch_tc<true, float>(args, maps, stream) : launch_tc<false, float>(args, maps, stream);
+    return packed ? launch_tc<true, bf16>(args, maps, stream) : launch_tc<false, bf16>(args, maps, stream);
 }
 
 }  // namespace awa

@@ -19,6 +19,7 @@ struct WindowDesc
     int nt, nh, nw;  // clipped extent
     int offset;      // first packed row (cu_seqlens[w])
     int video;       // nt * nh * nw
+    int h0n, w0n;    // start of the unclipped (nominal-size) window: < h0, w0 only where clipped at 0
 };
 
 // Device tables of a plan (uploaded once by awa_plan_create).
@@ -39,6 +40,16 @@ struct PlanDevice
     int rope_dim = 0;
     int pairs_per_axis = 0;  // rope_dim / 6
     int max_coord = 0;
+    // Slab geometry of the tcgen05 kernel's fused path. A window's video rows
+    // are fetched as boxes of tc_bhc x tc_bwc (h x w) tokens of one frame,
+    // laid over the nominal window (tc_bh x tc_bw from (h0n, w0n)); every box
+    // fills one 64-row key block (tc_rows rows used). Text rows follow in
+    // blocks of 64 rows.
+    int tc_bh = 0, tc_bw = 0;    // nominal window extent in h, w
+    int tc_bhc = 0, tc_bwc = 0;  // box extent in h, w
+    int tc_nhc = 0, tc_nwc = 0;  // boxes per frame along h, w
+    int tc_rows = 0;             // tc_bhc * tc_bwc <= 64
+    int tc_text_blocks = 0;      // ceil(text_tokens / 64)
 };
 
 enum DType : int

@@ -34,14 +34,16 @@ struct awa_plan
     std::vector<float2> rope_table;
     std::vector<uint32_t> rope_table_bf16;  // per (coord, pair): bf16 cos (low half), bf16 sin (high half)
     std::vector<short4> position_coords;
-    std::vector<int2> items_tc;    // (window, pair of 128-row q tiles), longest windows first
-    std::vector<int2> items_simt;  // (window, 64-row q tile)
-    std::vector<int> item_window_begin_tc;  // items_tc index of the first item of each window (plan order)
-    std::vector<double> window_cost;        // L^2 per window
+    std::vector<int2> items_tc;         // fused tcgen05 path: (window, pair of 128-row q tiles), longest first
+    std::vector<int2> items_tc_packed;  // packed tcgen05 path: same, over the packed rows
+    std::vector<int2> items_simt;       // (window, 64-row q tile)
+    std::vector<double> window_cost;    // L^2 per window
+    bool tc_slabs = false;              // every window is a clipped piece of a nominal-size window
     // device copies
     PlanDevice dev{};
     void* device_block = nullptr;
     const int2* d_items_tc = nullptr;
+    const int2* d_items_tc_packed = nullptr;
     const int2* d_items_simt = nullptr;
     std::mutex range_mutex;  // guards the per-range item cache below
     std::vector<std::pair<std::pair<int, int>, std::pair<int2*, int>>> range_items;  // (begin,end) -> items
@@ -366,16 +368,56 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
         }
     }
 
+    // Slab geometry of the tcgen05 kernel. The window rule tiles each axis
+    // with windows of one nominal size, clipped only at the grid's edges, so
+    // laying a nominal-size box over each window reads nothing of another
+    // window: the part of the box outside the window lies outside the grid.
+    // Checked for every window; without it the SIMT kernel runs.
+    {
+        int bh = 0, bw = 0;
+        for (const WindowDesc& d : plan->descs)
+        {
+            bh = std::max(bh, d.nh);
+            bw = std::max(bw, d.nw);
+        }
+        auto nominal_start = [](int start, int count, int size) { return start == 0 ? start + count - size : start; };
+        bool ok = true;
+        for (WindowDesc& d : plan->descs)
+        {
+            d.h0n = nominal_start(d.h0, d.nh, bh);
+            d.w0n = nominal_start(d.w0, d.nw, bw);
+            // the box [x0n, x0n + size) clipped to the grid must be exactly the window
+            ok = ok && std::max(d.h0n, 0) == d.h0 && std::min(d.h0n + bh, sh) == d.h0 + d.nh &&
+                 std::max(d.w0n, 0) == d.w0 && std::min(d.w0n + bw, sw) == d.w0 + d.nw;
+        }
+        PlanDevice& g = plan->dev;
+        g.tc_bh = bh;
+        g.tc_bw = bw;
+        g.tc_bwc = std::min(bw, 64);
+        g.tc_bhc = std::max(1, std::min(bh, 64 / g.tc_bwc));
+        g.tc_nhc = ceil_div(bh, g.tc_bhc);
+        g.tc_nwc = ceil_div(bw, g.tc_bwc);
+        g.tc_rows = g.tc_bhc * g.tc_bwc;
+        g.tc_text_blocks = ceil_div(text, 64);
+        plan->tc_slabs = ok && bh <= 256 && bw <= 256;
+    }
+
     // Work lists, longest windows first so the tail of the grid is short.
+    // tcgen05 items are pairs of 128-row query tiles = 4 key blocks of 64 rows.
     std::vector<int> order(window_count);
     for (int i = 0; i < window_count; i++)
         order[i] = i;
     std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return plan->window_cost[a] > plan->window_cost[b]; });
+    const PlanDevice& g = plan->dev;
     for (int w : order)
     {
-        const int length = plan->descs[w].video + text;
-        for (int q = 0; q < ceil_div(length, 2 * awa::kTcRowsPerTile); q++)
+        const WindowDesc& d = plan->descs[w];
+        const int length = d.video + text;
+        const int fused_blocks = d.nt * g.tc_nhc * g.tc_nwc + g.tc_text_blocks;
+        for (int q = 0; q < ceil_div(fused_blocks, 4); q++)
             plan->items_tc.push_back(make_int2(w, q));
+        for (int q = 0; q < ceil_div(length, 4 * 64); q++)
+            plan->items_tc_packed.push_back(make_int2(w, q));
         for (int q = 0; q < ceil_div(length, awa::kSimtRowsPerTile); q++)
             plan->items_simt.push_back(make_int2(w, q));
     }
@@ -404,12 +446,15 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
         delete plan;
         return cuda_fail(err, "cudaGetDevice");
     }
-    size_t offsets[9];
+    constexpr int kSegments = 10;
+    size_t offsets[kSegments];
     size_t total = 0;
-    const size_t sizes[9] = {bytes_of(plan->descs),        bytes_of(plan->sequence_index),  bytes_of(plan->cu_seqlens),
-                             bytes_of(plan->video_positions), bytes_of(plan->position_coords), bytes_of(plan->rope_table),
-                             bytes_of(plan->items_tc),     bytes_of(plan->items_simt),      bytes_of(plan->rope_table_bf16)};
-    for (int i = 0; i < 9; i++)
+    const size_t sizes[kSegments] = {
+        bytes_of(plan->descs),           bytes_of(plan->sequence_index), bytes_of(plan->cu_seqlens),
+        bytes_of(plan->video_positions), bytes_of(plan->position_coords), bytes_of(plan->rope_table),
+        bytes_of(plan->items_tc),        bytes_of(plan->items_simt),      bytes_of(plan->rope_table_bf16),
+        bytes_of(plan->items_tc_packed)};
+    for (int i = 0; i < kSegments; i++)
     {
         offsets[i] = total;
         total = align_up(total + sizes[i], 256);
@@ -421,10 +466,12 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
         return cuda_fail(err, "cudaMalloc(plan tables)");
     }
     std::vector<unsigned char> staging(total, 0);
-    const void* sources[9] = {plan->descs.data(),           plan->sequence_index.data(), plan->cu_seqlens.data(),
-                              plan->video_positions.data(), plan->position_coords.data(), plan->rope_table.data(),
-                              plan->items_tc.data(),        plan->items_simt.data(),      plan->rope_table_bf16.data()};
-    for (int i = 0; i < 9; i++)
+    const void* sources[kSegments] = {
+        plan->descs.data(),           plan->sequence_index.data(),  plan->cu_seqlens.data(),
+        plan->video_positions.data(), plan->position_coords.data(), plan->rope_table.data(),
+        plan->items_tc.data(),        plan->items_simt.data(),      plan->rope_table_bf16.data(),
+        plan->items_tc_packed.data()};
+    for (int i = 0; i < kSegments; i++)
         if (sizes[i])
             std::memcpy(staging.data() + offsets[i], sources[i], sizes[i]);
     err = cudaMemcpy(plan->device_block, staging.data(), total, cudaMemcpyHostToDevice);
@@ -445,6 +492,7 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
     dev.rope_table_bf16 = reinterpret_cast<const uint32_t*>(base + offsets[8]);
     plan->d_items_tc = reinterpret_cast<const int2*>(base + offsets[6]);
     plan->d_items_simt = reinterpret_cast<const int2*>(base + offsets[7]);
+    plan->d_items_tc_packed = reinterpret_cast<const int2*>(base + offsets[9]);
     dev.source_t = st;
     dev.source_h = sh;
     dev.source_w = sw;
@@ -553,13 +601,15 @@ int awa_mmrope(const awa_plan* plan, int heads, int head_dim, int in_dtype, cons
                          "awa_mmrope launch");
 }
 
-int awa_attention_kernel_kind(const awa_plan* plan, int precision, int heads, int head_dim)
+int awa_attention_kernel_kind(const awa_plan* plan, int precision, int in_dtype, int heads, int head_dim)
 {
     (void)heads;
     // The tcgen05 kernel keeps the (coordinate, pair) RoPE table in 16 KB of
     // shared memory: 4096 entries, i.e. window extents up to ~195 at rope_dim 126.
     const bool table_fits = plan && (long long)plan->max_coord * plan->pairs_per_axis <= 4096;
-    return precision == AWA_PREC_BF16 && head_dim == 128 && table_fits ? 1 : 2;
+    return precision == AWA_PREC_BF16 && in_dtype == AWA_BF16 && head_dim == 128 && table_fits && plan->tc_slabs
+               ? 1
+               : 2;
 }
 
 static int run_attention(const awa_plan* plan, int precision, awa::AttnArgs& args, int packed, int in_dtype,
@@ -572,7 +622,7 @@ static int run_attention(const awa_plan* plan, int precision, awa::AttnArgs& arg
     args.item_count = item_count;
     if (item_count == 0)
         return AWA_OK;
-    if (awa_attention_kernel_kind(plan, precision, args.heads, args.head_dim) == 1)
+    if (awa_attention_kernel_kind(plan, precision, in_dtype, args.heads, args.head_dim) == 1)
         return launch_status(awa::launch_attention_tc(args, packed, in_dtype, out_dtype, stream), "tcgen05 attention");
     return launch_status(awa::launch_attention_simt(args, packed, in_dtype, out_dtype, stream), "simt attention");
 }
@@ -601,12 +651,13 @@ int awa_window_attention(const awa_plan* plan, int precision, int heads, int hea
     args.qkv_token_stride = in_token_stride;
     args.out = attended;
     args.out_token_stride = out_token_stride;
-    const bool tc = awa_attention_kernel_kind(plan, precision, heads, head_dim) == 1;
+    const bool tc = awa_attention_kernel_kind(plan, precision, in_dtype, heads, head_dim) == 1;
     if (tc && (!is_aligned16(packed) || !is_aligned16(attended) || (in_token_stride * dtype_size(in_dtype)) % 16 ||
                (out_token_stride * dtype_size(out_dtype)) % 16))
         return fail(AWA_ERR_INVALID, "awa_window_attention: bf16 tensor-core path needs 16-byte aligned rows");
-    return run_attention(plan, precision, args, 1, in_dtype, out_dtype, tc ? plan->d_items_tc : plan->d_items_simt,
-                         static_cast<int>(tc ? plan->items_tc.size() : plan->items_simt.size()), stream);
+    return run_attention(plan, precision, args, 1, in_dtype, out_dtype,
+                         tc ? plan->d_items_tc_packed : plan->d_items_simt,
+                         static_cast<int>(tc ? plan->items_tc_packed.size() : plan->items_simt.size()), stream);
 }
 
 int awa_unpack(const awa_plan* plan, int heads, int head_dim, int in_dtype, const void* attended,
@@ -694,7 +745,7 @@ static int forward_impl(const awa_plan* cplan, int precision, int heads, int hea
     const size_t need = (size_t)(window_end - window_begin) * plan->info.text_tokens * head_row * sizeof(float);
     if (!workspace || workspace_bytes < need)
         return fail(AWA_ERR_INVALID, "awa_forward: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
-    const bool tc = awa_attention_kernel_kind(plan, precision, heads, head_dim) == 1;
+    const bool tc = awa_attention_kernel_kind(plan, precision, in_dtype, heads, head_dim) == 1;
     if (tc)
     {
         const size_t in_size = dtype_size(in_dtype), out_size = dtype_size(out_dtype);
