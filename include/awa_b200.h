@@ -154,6 +154,40 @@ int awa_forward(const awa_plan* plan, int precision, int heads, int head_dim, in
                 int64_t video_token_stride_out, void* text_out, int64_t text_token_stride_out, void* workspace,
                 size_t workspace_bytes, awa_stream_t stream);
 
+/* Size of the scratch that awa_forward_noalloc uses: 32 MiB of device memory
+ * per GPU that loads this library, held until the process exits. */
+#define AWA_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* awa_forward for callers that must not allocate device memory. Some hosts
+ * cannot let a library call cudaMalloc: an inference server whose memory
+ * manager reserves the whole GPU up front and owns every byte, a plugin whose
+ * host framework hands out device memory only through its own allocator, or
+ * a latency-bound pipeline that cannot afford the device-wide
+ * synchronisation cudaMalloc/cudaFree cause. awa_forward needs the caller to
+ * pass a workspace; this entry point instead uses a fixed scratch array that
+ * the library holds in device memory (AWA_NOALLOC_SCRATCH_BYTES per GPU), and
+ * it allocates nothing. No counterpart in the reference (its layers take
+ * scratch from ncnn's workspace allocator).
+ *   - Arguments, outputs and results are those of awa_forward, minus the
+ *     workspace.
+ *   - Limit: the layer's workspace (awa_forward_workspace_bytes) must fit in
+ *     AWA_NOALLOC_SCRATCH_BYTES, e.g. 56 windows at 58 text tokens, 20 heads,
+ *     head_dim 128. Larger layers get AWA_ERR_INVALID and a message; use
+ *     awa_forward with a workspace for them.
+ *   - The first call on a device looks up the scratch's device address (with
+ *     that device current; it must be the plan's device). Make that first
+ *     call before any stream capture begins.
+ *   - All calls on a GPU share the one scratch array, which keeps the last
+ *     call's contents. Nothing in it needs to start at zero (each call writes
+ *     every value it later reads), but calls that overlap on the GPU (other
+ *     streams, other threads) race on it: order them on one stream or with
+ *     events. */
+int awa_forward_noalloc(const awa_plan* plan, int precision, int heads, int head_dim, int in_dtype,
+                        const void* video_qkv, int64_t video_token_stride, int64_t video_qkv_stride,
+                        const void* text_qkv, int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype,
+                        void* video_out, int64_t video_token_stride_out, void* text_out,
+                        int64_t text_token_stride_out, awa_stream_t stream);
+
 /* Window-parallel form of awa_forward for one rank of a multi-GPU group:
  * computes only the windows [window_begin, window_end) of the plan's window
  * order (every token of those windows is written to video_out; other rows

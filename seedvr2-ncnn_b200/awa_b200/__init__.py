@@ -30,11 +30,13 @@ AWA_ERR_INVALID = -1
 AWA_ERR_CUDA = -2
 AWA_ERR_DEVICE = -3
 AWA_ERR_ALLOC = -100
+AWA_NOALLOC_SCRATCH_BYTES = 32 << 20  # scratch of awa_forward_noalloc, per GPU
 
 # Every symbol declared in include/awa_b200.h.
 EXPORTED_SYMBOLS = (
     "awa_make_windows", "awa_plan_create", "awa_plan_create_host", "awa_plan_destroy", "awa_plan_get_info", "awa_plan_get_maps",
     "awa_pack", "awa_mmrope", "awa_window_attention", "awa_unpack", "awa_forward_workspace_bytes", "awa_forward",
+    "awa_forward_noalloc",
     "awa_forward_windows", "awa_text_finalize", "awa_scatter_video_shard", "awa_gather_video_shard",
     "awa_window_range_video_rows", "awa_partition_windows", "awa_device_status", "awa_attention_kernel_kind",
     "awa_profile_enable", "awa_profile_reset", "awa_profile_collect", "awa_last_error", "awa_version",
@@ -91,6 +93,7 @@ def library() -> ctypes.CDLL:
         "awa_unpack": (i, [p, i, i, i, p, i64, i, p, i64, p, i64, p]),
         "awa_forward_workspace_bytes": (sz, [p, i, i]),
         "awa_forward": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p, sz, p]),
+        "awa_forward_noalloc": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p]),
         "awa_forward_windows": (i, [p, i, i, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, p, sz, p]),
         "awa_text_finalize": (i, [p, i, i, p, i, p, i64, p]),
         "awa_scatter_video_shard": (i, [p, i, i, i, i, i, p, p, i64, p]),

@@ -118,6 +118,8 @@ int launch_attention_simt(const AttnArgs& args, int packed, int in_dtype, int ou
 int launch_attention_tc(const AttnArgs& args, int packed, int in_dtype, int out_dtype, cudaStream_t stream);
 
 int* device_error_flag();  // per-device flag in device memory
+// Sets the calling thread's awa_last_error() text; returns code.
+int report_error(int code, const char* message);
 
 // Launch profiler: ProfileScope brackets one launch with events when enabled.
 bool profiling_enabled();

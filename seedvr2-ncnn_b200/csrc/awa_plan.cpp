@@ -198,6 +198,11 @@ int launch_status(int err, const char* what)
 namespace awa
 {
 
+int report_error(int code, const char* message)
+{
+    return fail(code, "%s", message);
+}
+
 int* device_error_flag()
 {
     static std::mutex mutex;
