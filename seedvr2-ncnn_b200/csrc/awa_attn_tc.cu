@@ -493,19 +493,21 @@ __device__ void tma_role(const AttnArgs& a, const TmaMaps& maps, TcShared& sh, i
 }
 
 // ---------------------------------------------------------------- RoPE warps
-// Shared-memory round trips are slow while the tensor core and TMA stream
-// through shared memory, so every step below first issues all of its loads
-// (data and RoPE table entries) and only then computes: one round trip per
-// batch instead of a dependent chain per row.
-template <bool PACKED>
+// Every step below first issues all of its loads (data and RoPE table
+// entries) and only then computes, and it never branches per pair: each pair
+// is rotated and the result selected. RD is the rotated width (rope_dim) as a
+// compile-time constant (126, the reference's default, with 21 pairs per
+// axis), or 0 to read it from the plan; a per-pair run-time test costs the
+// loop several times its arithmetic.
+template <bool PACKED, int RD>
 __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t tmem)
 {
     const int ptid = threadIdx.x - kRopeWarp0 * 32;  // = this thread's TMEM lane / Q row
     const uint32_t lane_base = (uint32_t)(ptid & ~31) << 16;
     const int c = ptid & 15;    // K chunk of this thread
     const int kr0 = ptid >> 4;  // K rows kr0 + 8 jj
-    const int ppa = a.plan.pairs_per_axis;
-    const int rope_dim = a.plan.rope_dim;
+    const int ppa = RD ? RD / 6 : a.plan.pairs_per_axis;
+    const int rope_dim = RD ? RD : a.plan.rope_dim;
     const int bwc = a.plan.tc_bwc > 0 ? a.plan.tc_bwc : 1;
     const uint32_t* table = sh.rope;
     volatile int* abort = &sh.abort;
@@ -597,12 +599,14 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
                     {
                         const int pair = 32 * h + k;  // features 2 pair, 2 pair + 1
                         const int b = pair < ppa ? base[0] : pair < 2 * ppa ? base[1] : base[2];
-                        cs[k] = 2 * pair < rope_dim ? table[b + pair] : 0u;
+                        cs[k] = table[2 * pair < rope_dim ? b + pair : 0];
                     }
 #pragma unroll
                     for (int k = 0; k < 32; k++)
-                        if (2 * (32 * h + k) < rope_dim)
-                            words[k] = rotate_bf16x2(words[k], cs[k]);
+                    {
+                        const uint32_t rotated = rotate_bf16x2(words[k], cs[k]);
+                        words[k] = 2 * (32 * h + k) < rope_dim ? rotated : words[k];
+                    }
                 }
                 tc::tmem_st32(tmem + lane_base + kColQ + 64u * t + 32u * h, words);
             }
@@ -660,8 +664,10 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
                     uint32_t words[4] = {data[jj].x, data[jj].y, data[jj].z, data[jj].w};
 #pragma unroll
                     for (int i = 0; i < 4; i++)
-                        if (k_active[i])
-                            words[i] = rotate_bf16x2(words[i], cs[jj][i]);
+                    {
+                        const uint32_t rotated = rotate_bf16x2(words[i], cs[jj][i]);
+                        words[i] = k_active[i] ? rotated : words[i];
+                    }
                     *reinterpret_cast<uint4*>(k_tile + swizzled_offset(kKeys, kr0 + 8 * jj, c)) =
                         make_uint4(words[0], words[1], words[2], words[3]);
                 }
@@ -973,7 +979,7 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
     }
 }
 
-template <bool PACKED, typename TOut>
+template <bool PACKED, typename TOut, int RD>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const AttnArgs a, const __grid_constant__ TmaMaps maps)
 {
@@ -1043,7 +1049,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp < kSoftmaxWarps)
         softmax_role<PACKED, TOut>(a, sh, njobs, tmem);
     else if (warp < kMmaWarp)
-        rope_role<PACKED>(a, sh, njobs, tmem);
+        rope_role<PACKED, RD>(a, sh, njobs, tmem);
     else if (warp == kMmaWarp)
         mma_role<PACKED>(a, sh, njobs, tmem);
     else
@@ -1154,11 +1160,11 @@ bool build_maps(const AttnArgs& a, int packed, TmaMaps& maps)
     return true;
 }
 
-template <bool PACKED, typename TOut>
+template <bool PACKED, typename TOut, int RD>
 int launch_tc(const AttnArgs& a, const TmaMaps& maps, cudaStream_t stream)
 {
     const size_t smem = sizeof(TcShared) + 1024;
-    auto kernel = attention_tc_kernel<PACKED, TOut>;
+    auto kernel = attention_tc_kernel<PACKED, TOut, RD>;
     cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess)
         return (int)err;
@@ -1183,9 +1189,17 @@ int launch_attention_tc(const AttnArgs& args, int packed, int in_dtype, int out_
     if (!build_maps(args, packed, maps))
         return (int)cudaErrorInvalidValue;
     ProfileScope prof(packed ? "awa_attention_tc_packed" : "awa_attention_tc_fused", stream);
+    // The packed path applies no RoPE; the fused path has a 126-wide (21 pairs per axis) instance.
+    const bool rd126 = p.rope_dim == 126 && p.pairs_per_axis == 21;
     if (out_dtype == kF32)
-        return packed ? launch_tc<true, float>(args, maps, stream) : launch_tc<false, float>(args, maps, stream);
-    return packed ? launch_tc<true, bf16>(args, maps, stream) : launch_tc<false, bf16>(args, maps, stream);
+    {
+        if (packed)
+            return launch_tc<true, float, 0>(args, maps, stream);
+        return rd126 ? launch_tc<false, float, 126>(args, maps, stream) : launch_tc<false, float, 0>(args, maps, stream);
+    }
+    if (packed)
+        return launch_tc<true, bf16, 0>(args, maps, stream);
+    return rd126 ? launch_tc<false, bf16, 126>(args, maps, stream) : launch_tc<false, bf16, 0>(args, maps, stream);
 }
 
 }  // namespace awa
