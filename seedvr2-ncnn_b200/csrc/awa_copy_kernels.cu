@@ -236,8 +236,26 @@ __global__ void text_reduce(PlanDevice plan, int head_row, int packed, const TIn
     {
         const int i = (int)(id / head_row);
         const int e = (int)(id - (int64_t)i * head_row);
+        // Eight windows' values are loaded before any is added (eight loads in
+        // flight per thread); the additions stay in window order.
+        constexpr int kBatch = 8;
         float acc = 0.f;
-        for (int w = window_begin; w < window_end; w++)
+        int w = window_begin;
+        for (; w + kBatch <= window_end; w += kBatch)
+        {
+            float x[kBatch];
+#pragma unroll
+            for (int u = 0; u < kBatch; u++)
+            {
+                const int64_t row = packed ? (int64_t)__ldg(plan.cu_seqlens + w + u + 1) - text + i
+                                           : (int64_t)(w + u - window_begin) * text + i;
+                x[u] = load1(src + row * sts + e);
+            }
+#pragma unroll
+            for (int u = 0; u < kBatch; u++)
+                acc = __fadd_rn(acc, divisor != 0.f ? __fdiv_rn(x[u], divisor) : x[u]);
+        }
+        for (; w < window_end; w++)
         {
             const int64_t row = packed ? (int64_t)__ldg(plan.cu_seqlens + w + 1) - text + i
                                        : (int64_t)(w - window_begin) * text + i;
