@@ -363,11 +363,6 @@ __device__ __forceinline__ uint32_t rotate_bf16x2(uint32_t w, uint32_t t)
     return out;
 }
 
-__device__ __forceinline__ int rope_axis(int pair, int ppa)
-{
-    return pair >= 2 * ppa ? 2 : pair >= ppa ? 1 : 0;
-}
-
 // Byte offset of 16-byte chunk c (0..15 along the 128 features) of row r in a
 // swizzled tile of `rows` rows: two 64-feature panels, 128-byte rows, chunk
 // XOR row%8 -- the layout the 128-byte-swizzle TMA writes from a 1024-byte
@@ -375,6 +370,67 @@ __device__ __forceinline__ int rope_axis(int pair, int ppa)
 __device__ __forceinline__ uint32_t swizzled_offset(int rows, int r, int c)
 {
     return (uint32_t)((c >> 3) * rows * 128 + r * 128 + ((((c & 7) ^ (r & 7))) << 4));
+}
+
+// Rotate 32 consecutive bf16 pairs (half a 128-feature row: pairs 32*HALF ..)
+// of one row whose table bases are base[x] = (coord_x - x) * ppa: the entry of
+// pair p on axis x is base[x] + p. Pairs at or past rope_dim / 2 pass
+// through. With RD != 0, the axis of every pair is a compile-time constant.
+template <int HALF, int RD>
+__device__ __forceinline__ void rotate_half_row(uint32_t (&words)[32], const int (&base)[3], const uint32_t* table,
+                                                int ppa_rt, int rope_dim_rt)
+{
+    const int ppa = RD ? RD / 6 : ppa_rt;
+    const int rope_dim = RD ? RD : rope_dim_rt;
+    uint32_t cs[32];
+#pragma unroll
+    for (int k = 0; k < 32; k++)
+    {
+        const int pair = 32 * HALF + k;  // features 2 pair, 2 pair + 1
+        const int b = pair < ppa ? base[0] : pair < 2 * ppa ? base[1] : base[2];
+        cs[k] = table[2 * pair < rope_dim ? b + pair : 0];
+    }
+#pragma unroll
+    for (int k = 0; k < 32; k++)
+    {
+        const uint32_t rotated = rotate_bf16x2(words[k], cs[k]);
+        words[k] = 2 * (32 * HALF + k) < rope_dim ? rotated : words[k];
+    }
+}
+
+// Table bases of a window row (see rotate_half_row); zero for rows that are
+// not window rows (their values are never used, any in-range entry will do).
+__device__ __forceinline__ void row_bases(int (&base)[3], bool valid, const BlockGeo& geo, int text, int row_h,
+                                          int row_w, int hoff, int woff, int row, int ppa)
+{
+    int ct = 0, ch = 1, cw = 2;
+    if (valid)
+    {
+        if (geo.video)
+        {
+            ct = text + geo.lt;
+            ch = geo.hb + row_h - hoff;
+            cw = geo.wb + row_w - woff;
+        }
+        else
+            ct = ch = cw = geo.first + row;
+    }
+    base[0] = ct * ppa;
+    base[1] = (ch - 1) * ppa;
+    base[2] = (cw - 2) * ppa;
+}
+
+__device__ __forceinline__ void load_half_row(uint32_t (&words)[32], const uint8_t* tile, int rows, int r, int half)
+{
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+    {
+        const uint4 w = *reinterpret_cast<const uint4*>(tile + swizzled_offset(rows, r, 8 * half + k));
+        words[4 * k + 0] = w.x;
+        words[4 * k + 1] = w.y;
+        words[4 * k + 2] = w.z;
+        words[4 * k + 3] = w.w;
+    }
 }
 
 // ---------------------------------------------------------------- MMA helpers
@@ -504,8 +560,8 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
 {
     const int ptid = threadIdx.x - kRopeWarp0 * 32;  // = this thread's TMEM lane / Q row
     const uint32_t lane_base = (uint32_t)(ptid & ~31) << 16;
-    const int c = ptid & 15;    // K chunk of this thread
-    const int kr0 = ptid >> 4;  // K rows kr0 + 8 jj
+    const int kr = ptid & 63;    // K row of this thread
+    const int khalf = ptid >> 6;  // ... and its half (features 64 khalf ..): warps 8-9 / 10-11
     const int ppa = RD ? RD / 6 : a.plan.pairs_per_axis;
     const int rope_dim = RD ? RD : a.plan.rope_dim;
     const int bwc = a.plan.tc_bwc > 0 ? a.plan.tc_bwc : 1;
@@ -514,23 +570,9 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
     uint32_t q_loaded_phase = 0;
     uint32_t q_empty_phase = 1;  // TMEM Q starts free
     uint32_t g = 0;
-    // per-thread constants of the K chunk: pairs 4c .. 4c+3
-    int k_axis[4], k_within[4];
-    bool k_active[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-    {
-        const int pair = 4 * c + i;
-        k_active[i] = 2 * pair < rope_dim;
-        k_axis[i] = rope_axis(pair, ppa);
-        k_within[i] = pair - k_axis[i] * ppa;
-    }
-    // (h, w) within a box of this thread's K rows kr0 + 8 jj and of its Q row
-    int k_hw[8];
-#pragma unroll
-    for (int jj = 0; jj < 8; jj++)
-        k_hw[jj] = ((kr0 + 8 * jj) / bwc) * 256 + (kr0 + 8 * jj) % bwc;
-    const int q_h = (ptid & 63) / bwc, q_w = (ptid & 63) % bwc;
+    // (h, w) within a box of block row ptid & 63 (this thread's Q row in its
+    // block, and its K row)
+    const int row_h = (ptid & 63) / bwc, row_w = (ptid & 63) % bwc;
 
     for (int j = blockIdx.x; j < njobs; j += gridDim.x)
     {
@@ -550,66 +592,23 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
             if (t == 1 && !job.has_b)
                 break;
             const uint8_t* tile = sh.q[t];
-            // table entry of pair p on axis x: base[x] + p (base[x] = (coord_x - x) * ppa)
             int base[3] = {0, 0, 0};
-            bool rotate = false;
             if (!PACKED)
             {
                 const int b = 2 * (job.qa + t) + (ptid >> 6);
-                if (b < job.blocks)
-                {
-                    const BlockGeo geo = block_geo<PACKED>(a, job, b);
-                    if ((block_mask<PACKED>(a, job, geo) >> (ptid & 63)) & 1ull)
-                    {
-                        int ct, ch, cw;
-                        if (geo.video)
-                        {
-                            ct = a.plan.text_tokens + geo.lt;
-                            ch = geo.hb + q_h - hoff;
-                            cw = geo.wb + q_w - woff;
-                        }
-                        else
-                            ct = ch = cw = geo.first + (ptid & 63);
-                        base[0] = ct * ppa;
-                        base[1] = (ch - 1) * ppa;
-                        base[2] = (cw - 2) * ppa;
-                        rotate = true;
-                    }
-                }
+                const BlockGeo geo = block_geo<PACKED>(a, job, b);
+                const bool valid = b < job.blocks && ((block_mask<PACKED>(a, job, geo) >> (ptid & 63)) & 1ull);
+                row_bases(base, valid, geo, a.plan.text_tokens, row_h, row_w, hoff, woff, ptid & 63, ppa);
             }
-            // half a row (8 chunks = 32 bf16 pairs = 32 TMEM columns) per batch
-#pragma unroll 1
-            for (int h = 0; h < 2; h++)
-            {
-                uint32_t words[32];
-#pragma unroll
-                for (int k = 0; k < 8; k++)
-                {
-                    const uint4 w = *reinterpret_cast<const uint4*>(tile + swizzled_offset(kQRows, ptid, 8 * h + k));
-                    words[4 * k + 0] = w.x;
-                    words[4 * k + 1] = w.y;
-                    words[4 * k + 2] = w.z;
-                    words[4 * k + 3] = w.w;
-                }
-                if (!PACKED && rotate)
-                {
-                    uint32_t cs[32];
-#pragma unroll
-                    for (int k = 0; k < 32; k++)
-                    {
-                        const int pair = 32 * h + k;  // features 2 pair, 2 pair + 1
-                        const int b = pair < ppa ? base[0] : pair < 2 * ppa ? base[1] : base[2];
-                        cs[k] = table[2 * pair < rope_dim ? b + pair : 0];
-                    }
-#pragma unroll
-                    for (int k = 0; k < 32; k++)
-                    {
-                        const uint32_t rotated = rotate_bf16x2(words[k], cs[k]);
-                        words[k] = 2 * (32 * h + k) < rope_dim ? rotated : words[k];
-                    }
-                }
-                tc::tmem_st32(tmem + lane_base + kColQ + 64u * t + 32u * h, words);
-            }
+            uint32_t words[32];
+            load_half_row(words, tile, kQRows, ptid, 0);
+            if (!PACKED)
+                rotate_half_row<0, RD>(words, base, table, ppa, rope_dim);
+            tc::tmem_st32(tmem + lane_base + kColQ + 64u * t, words);
+            load_half_row(words, tile, kQRows, ptid, 1);
+            if (!PACKED)
+                rotate_half_row<1, RD>(words, base, table, ppa, rope_dim);
+            tc::tmem_st32(tmem + lane_base + kColQ + 64u * t + 32u, words);
         }
         tc::tmem_wait_st();
         tc::fence_before_sync();
@@ -629,60 +628,32 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
                 return;
             if (!PACKED)
             {
+                // one row, half its features, per thread (same shape as the Q step)
                 uint8_t* k_tile = sh.kv[stage][0];
-                uint4 data[8];
+                int base[3];
+                row_bases(base, (mask >> kr) & 1ull, geo, a.plan.text_tokens, row_h, row_w, hoff, woff, kr, ppa);
+                uint32_t words[32];
+                load_half_row(words, k_tile, kKeys, kr, khalf);
+                if (khalf == 0)
+                    rotate_half_row<0, RD>(words, base, table, ppa, rope_dim);
+                else
+                    rotate_half_row<1, RD>(words, base, table, ppa, rope_dim);
 #pragma unroll
-                for (int jj = 0; jj < 8; jj++)
-                    data[jj] = *reinterpret_cast<const uint4*>(k_tile + swizzled_offset(kKeys, kr0 + 8 * jj, c));
-                uint32_t cs[8][4];
-#pragma unroll
-                for (int jj = 0; jj < 8; jj++)
-                {
-                    const int r = kr0 + 8 * jj;
-                    const bool valid = (mask >> r) & 1ull;
-                    int co[3];
-                    if (geo.video)
-                    {
-                        co[0] = a.plan.text_tokens + geo.lt;
-                        co[1] = geo.hb + (k_hw[jj] >> 8) - hoff;
-                        co[2] = geo.wb + (k_hw[jj] & 255) - woff;
-                    }
-                    else
-                        co[0] = co[1] = co[2] = geo.first + r;
-#pragma unroll
-                    for (int i = 0; i < 4; i++)
-                    {
-                        const int axis = k_axis[i];
-                        const int coord = axis == 0 ? co[0] : axis == 1 ? co[1] : co[2];
-                        // rows outside the window are masked keys: any in-range entry will do
-                        cs[jj][i] = table[valid && k_active[i] ? coord * ppa + k_within[i] : 0];
-                    }
-                }
-#pragma unroll
-                for (int jj = 0; jj < 8; jj++)
-                {
-                    uint32_t words[4] = {data[jj].x, data[jj].y, data[jj].z, data[jj].w};
-#pragma unroll
-                    for (int i = 0; i < 4; i++)
-                    {
-                        const uint32_t rotated = rotate_bf16x2(words[i], cs[jj][i]);
-                        words[i] = k_active[i] ? rotated : words[i];
-                    }
-                    *reinterpret_cast<uint4*>(k_tile + swizzled_offset(kKeys, kr0 + 8 * jj, c)) =
-                        make_uint4(words[0], words[1], words[2], words[3]);
-                }
+                for (int k = 0; k < 8; k++)
+                    *reinterpret_cast<uint4*>(k_tile + swizzled_offset(kKeys, kr, 8 * khalf + k)) =
+                        make_uint4(words[4 * k], words[4 * k + 1], words[4 * k + 2], words[4 * k + 3]);
                 // generic-proxy writes -> visible to the tensor core's async-proxy reads
                 tc::fence_async_smem();
             }
             else if (mask != ~0ull)
             {
                 uint8_t* v_tile = sh.kv[stage][1];
-#pragma unroll
-                for (int jj = 0; jj < 8; jj++)
+                if (!((mask >> kr) & 1ull))
                 {
-                    const int r = kr0 + 8 * jj;
-                    if (!((mask >> r) & 1ull))
-                        *reinterpret_cast<uint4*>(v_tile + swizzled_offset(kKeys, r, c)) = make_uint4(0, 0, 0, 0);
+#pragma unroll
+                    for (int k = 0; k < 8; k++)
+                        *reinterpret_cast<uint4*>(v_tile + swizzled_offset(kKeys, kr, 8 * khalf + k)) =
+                            make_uint4(0, 0, 0, 0);
                 }
                 tc::fence_async_smem();
             }
