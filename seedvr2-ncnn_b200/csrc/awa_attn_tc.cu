@@ -122,14 +122,33 @@ struct Job
     bool has_b;   // second query tile exists
 };
 
+// The global-memory part of a job (its work item and window). Every role
+// fetches the next job's while it works on the current one: the two dependent
+// loads cost about a microsecond, which would otherwise stall each role at
+// every job boundary.
+struct JobSource
+{
+    int2 item;
+    WindowDesc win;
+};
+
+__device__ __forceinline__ JobSource fetch_job(const AttnArgs& a, int j, int njobs)
+{
+    JobSource src;
+    const int i = j < njobs ? j / a.heads : 0;
+    src.item = a.items[i];
+    src.win = a.plan.windows[src.item.x];
+    return src;
+}
+
 template <bool PACKED>
-__device__ __forceinline__ Job decode_job(const AttnArgs& a, int j)
+__device__ __forceinline__ Job decode_job(const AttnArgs& a, int j, const JobSource& src)
 {
     Job job;
-    const int2 item = a.items[j / a.heads];
+    const int2 item = src.item;
     job.head = j - (j / a.heads) * a.heads;
     job.window = item.x;
-    job.win = a.plan.windows[item.x];
+    job.win = src.win;
     job.length = job.win.video + a.plan.text_tokens;
     if (PACKED)
     {
@@ -326,6 +345,15 @@ __device__ __forceinline__ void load_block_panel(const AttnArgs& a, const TmaMap
         tma_load_2d(dst, &maps.map[1][m], x, g.first, bar);
 }
 
+// 32-byte global store (sm_100): eight 32-bit words at a 32-byte aligned address.
+__device__ __forceinline__ void st_global_v8(void* p, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3, uint32_t r4,
+                                             uint32_t r5, uint32_t r6, uint32_t r7)
+{
+    asm volatile("st.global.L1::no_allocate.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(r0), "r"(r1),
+                 "r"(r2), "r"(r3), "r"(r4), "r"(r5), "r"(r6), "r"(r7)
+                 : "memory");
+}
+
 // Barrier over the 128 RoPE threads that also ANDs their flags, so a wait
 // that gave up in one thread makes every RoPE thread leave together.
 __device__ __forceinline__ bool rope_all(bool ok)
@@ -491,9 +519,11 @@ __device__ void tma_role(const AttnArgs& a, const TmaMaps& maps, TcShared& sh, i
     uint32_t q_issued = 0;      // Q loads issued so far
     uint32_t g = 0;             // K/V blocks issued so far
     bool ok = true;
+    JobSource next = fetch_job(a, blockIdx.x, njobs);
     for (int j = blockIdx.x; j < njobs && ok; j += gridDim.x)
     {
-        const Job job = decode_job<PACKED>(a, j);
+        const Job job = decode_job<PACKED>(a, j, next);
+        next = fetch_job(a, j + gridDim.x, njobs);
         // ---- the job's Q tiles (up to 4 blocks) into the staging area
         if (!warp_all(wait_bar(&sh.bar.q_free, q_free_phase, abort, a.error_flag, 41)))
             break;
@@ -574,9 +604,11 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
     // block, and its K row)
     const int row_h = (ptid & 63) / bwc, row_w = (ptid & 63) % bwc;
 
+    JobSource next = fetch_job(a, blockIdx.x, njobs);
     for (int j = blockIdx.x; j < njobs; j += gridDim.x)
     {
-        const Job job = decode_job<PACKED>(a, j);
+        const Job job = decode_job<PACKED>(a, j, next);
+        next = fetch_job(a, j + gridDim.x, njobs);
         const int hoff = job.win.h0 - job.win.h0n, woff = job.win.w0 - job.win.w0n;
         // ---- Q: staging -> (rotate) -> TMEM
         if (!rope_all(wait_bar(&sh.bar.q_loaded, q_loaded_phase, abort, a.error_flag, 11)))
@@ -676,9 +708,11 @@ __device__ void mma_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t tm
     const uint32_t tmem_s[2] = {tmem + kColS, tmem + kColS + 64};
     const uint32_t tmem_o[2] = {tmem + kColO, tmem + kColO + 128};
     bool ok = true;
+    JobSource next = fetch_job(a, blockIdx.x, njobs);
     for (int j = blockIdx.x; j < njobs && ok; j += gridDim.x)
     {
-        const Job job = decode_job<PACKED>(a, j);
+        const Job job = decode_job<PACKED>(a, j, next);
+        next = fetch_job(a, j + gridDim.x, njobs);
         const int slots = job.has_b ? 2 : 1;
         if (!warp_all(wait_bar(&sh.bar.q_full, q_full_phase, abort, a.error_flag, 21)))
             break;
@@ -783,9 +817,11 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
     volatile int* abort = &sh.abort;
     uint32_t s_phase = 0;
     uint32_t pv_count = 0;  // PV MMAs of this slot issued so far (o_full completions)
+    JobSource next = fetch_job(a, blockIdx.x, njobs);
     for (int j = blockIdx.x; j < njobs; j += gridDim.x)
     {
-        const Job job = decode_job<PACKED>(a, j);
+        const Job job = decode_job<PACKED>(a, j, next);
+        next = fetch_job(a, j + gridDim.x, njobs);
         if (slot == 1 && !job.has_b)
             continue;
         // this thread's query row: row i of block qb
@@ -916,32 +952,49 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
             tc::tmem_wait_ld();
             if (dst >= 0)
             {
-                if (!PACKED && text_row)
+                // this thread's row: 64 fp32 (text partials, fp32 out) or bf16 values
+                const bool f32 = (!PACKED && text_row) || sizeof(TOut) == 4;
+                char* row = (!PACKED && text_row) ? reinterpret_cast<char*>(a.text_partial + dst + h * 64)
+                                                  : static_cast<char*>(a.out) + (dst + h * 64) * (int64_t)sizeof(TOut);
+                if (f32)
                 {
-                    float4* out = reinterpret_cast<float4*>(a.text_partial + dst + h * 64);
 #pragma unroll
-                    for (int i = 0; i < 16; i++)
-                        out[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
-                                             __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
-                }
-                else if (sizeof(TOut) == 4)
-                {
-                    float4* out = reinterpret_cast<float4*>(static_cast<float*>(a.out) + dst + h * 64);
+                    for (int i = 0; i < 64; i++)
+                        o[i] = __float_as_uint(__uint_as_float(o[i]) * inv);
+                    if (a.out_v8)
+                    {
 #pragma unroll
-                    for (int i = 0; i < 16; i++)
-                        out[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
-                                             __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+                        for (int i = 0; i < 8; i++)
+                            st_global_v8(row + 32 * i, o[8 * i], o[8 * i + 1], o[8 * i + 2], o[8 * i + 3], o[8 * i + 4],
+                                         o[8 * i + 5], o[8 * i + 6], o[8 * i + 7]);
+                    }
+                    else
+                    {
+#pragma unroll
+                        for (int i = 0; i < 16; i++)
+                            reinterpret_cast<uint4*>(row)[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+                    }
                 }
                 else
                 {
-                    uint4* out = reinterpret_cast<uint4*>(static_cast<bf16*>(a.out) + dst + h * 64);
+                    uint32_t pk[32];
 #pragma unroll
-                    for (int i = 0; i < 8; i++)
-                        out[i] = make_uint4(
-                            pack_bf16x2(__uint_as_float(o[8 * i]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
-                            pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv),
-                            pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv),
-                            pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
+                    for (int i = 0; i < 32; i++)
+                        pk[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+                    if (a.out_v8)
+                    {
+#pragma unroll
+                        for (int i = 0; i < 4; i++)
+                            st_global_v8(row + 32 * i, pk[8 * i], pk[8 * i + 1], pk[8 * i + 2], pk[8 * i + 3],
+                                         pk[8 * i + 4], pk[8 * i + 5], pk[8 * i + 6], pk[8 * i + 7]);
+                    }
+                    else
+                    {
+#pragma unroll
+                        for (int i = 0; i < 8; i++)
+                            reinterpret_cast<uint4*>(row)[i] =
+                                make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+                    }
                 }
             }
         }
@@ -1159,18 +1212,22 @@ int launch_attention_tc(const AttnArgs& args, int packed, int in_dtype, int out_
     TmaMaps maps;
     if (!build_maps(args, packed, maps))
         return (int)cudaErrorInvalidValue;
+    AttnArgs a = args;
+    const int64_t out_size = out_dtype == kF32 ? 4 : 2;
+    a.out_v8 = (reinterpret_cast<uintptr_t>(args.out) % 32 == 0) && (args.out_token_stride * out_size) % 32 == 0 &&
+               (reinterpret_cast<uintptr_t>(args.text_partial) % 32 == 0) && (args.heads * args.head_dim * 4) % 32 == 0;
     ProfileScope prof(packed ? "awa_attention_tc_packed" : "awa_attention_tc_fused", stream);
     // The packed path applies no RoPE; the fused path has a 126-wide (21 pairs per axis) instance.
     const bool rd126 = p.rope_dim == 126 && p.pairs_per_axis == 21;
     if (out_dtype == kF32)
     {
         if (packed)
-            return launch_tc<true, float, 0>(args, maps, stream);
-        return rd126 ? launch_tc<false, float, 126>(args, maps, stream) : launch_tc<false, float, 0>(args, maps, stream);
+            return launch_tc<true, float, 0>(a, maps, stream);
+        return rd126 ? launch_tc<false, float, 126>(a, maps, stream) : launch_tc<false, float, 0>(a, maps, stream);
     }
     if (packed)
-        return launch_tc<true, bf16, 0>(args, maps, stream);
-    return rd126 ? launch_tc<false, bf16, 126>(args, maps, stream) : launch_tc<false, bf16, 0>(args, maps, stream);
+        return launch_tc<true, bf16, 0>(a, maps, stream);
+    return rd126 ? launch_tc<false, bf16, 126>(a, maps, stream) : launch_tc<false, bf16, 0>(a, maps, stream);
 }
 
 }  // namespace awa

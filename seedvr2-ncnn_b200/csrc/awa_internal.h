@@ -90,6 +90,7 @@ struct AttnArgs
     int item_count = 0;
     int window_begin = 0;  // fused, sharded: first window of this launch
     int* error_flag = nullptr;
+    int out_v8 = 0;  // tcgen05 kernel: output rows (and text partials) are 32-byte aligned
 };
 
 // Launchers (return a cudaError_t value as int).
