@@ -466,13 +466,17 @@ __device__ __forceinline__ void load_half_row(uint32_t (&words)[32], const uint8
 // K-major swizzled tile, 8 MMAs of K = 16 over the 128 features.
 __device__ __forceinline__ void issue_qk(uint32_t tmem_s, uint32_t tmem_q, uint32_t k_addr, int n)
 {
+    // The descriptor is built once; each K step only moves its start address
+    // field (address >> 4): one add between MMAs keeps the issuing thread ahead
+    // of the tensor core.
     const uint32_t idesc = tc::idesc_bf16_f32(128, n, false);
+    const uint64_t desc = tc::smem_desc_sw128(k_addr, 16, 1024);
 #pragma unroll
     for (int ks = 0; ks < 8; ks++)
     {
-        const uint32_t off = (uint32_t)((ks >> 2) * kKvPanel + (ks & 3) * 32);
-        tc::mma_ts(tmem_s, tmem_q + (uint32_t)(ks * 8), tc::smem_desc_sw128(k_addr + off, 16, 1024), idesc,
-                   ks > 0 ? 1u : 0u);
+        constexpr uint32_t kPanelStep = kKvPanel >> 4;
+        const uint64_t step = (uint64_t)((ks >> 2) * kPanelStep + (ks & 3) * 2);
+        tc::mma_ts(tmem_s, tmem_q + (uint32_t)(ks * 8), desc + step, idesc, ks > 0 ? 1u : 0u);
     }
 }
 
@@ -481,10 +485,13 @@ __device__ __forceinline__ void issue_qk(uint32_t tmem_s, uint32_t tmem_q, uint3
 __device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t tmem_p, uint32_t v_addr, int n, bool accumulate)
 {
     const uint32_t idesc = tc::idesc_bf16_f32(128, 128, true);
-    for (int ks = 0; ks < n / 16; ks++)
-        tc::mma_ts(tmem_o, tmem_p + (uint32_t)(ks * 8),
-                   tc::smem_desc_sw128(v_addr + (uint32_t)(ks * 2048), kKvPanel, 1024), idesc,
-                   (accumulate || ks > 0) ? 1u : 0u);
+    const uint64_t desc = tc::smem_desc_sw128(v_addr, kKvPanel, 1024);
+    const int steps = n / 16;
+#pragma unroll
+    for (int ks = 0; ks < kKeys / 16; ks++)
+        if (ks < steps)
+            tc::mma_ts(tmem_o, tmem_p + (uint32_t)(ks * 8), desc + (uint64_t)(ks * (2048 >> 4)), idesc,
+                       (accumulate || ks > 0) ? 1u : 0u);
 }
 
 // Rows the loads of block b write: a video box writes tc_rows of the 64.
