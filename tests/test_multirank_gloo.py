@@ -1,0 +1,123 @@
+"""Two-rank (gloo, CPU) test of the window-parallel multi-GPU protocol.
+
+On GPUs, rank r computes windows [bounds[r], bounds[r+1]) of
+awa_partition_windows with awa_forward_windows (its video rows + an
+unnormalised fp32 text partial sum), the ranks all-reduce the partial and
+call awa_text_finalize (divide by the window count). Here each rank runs the
+same protocol on the CPU with the oracle standing in for the kernels: the
+window split comes from the library's host-side plan, the exchange is a real
+gloo all-reduce / all-gather between two processes, and the result must equal
+the single-process reference chain (video rows bit-exact, text within the
+fp32 tolerance: the cross-rank sum adds in a different order).
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from awa_testlib import FP32_REL_L2, rel_l2
+
+CASES = [
+    # grid, window counts, shifted, heads, head_dim, text tokens
+    ((2, 16, 16), (1, 2, 2), True, 2, 16, 6),
+    ((3, 12, 20), (2, 3, 4), False, 2, 32, 5),
+]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _config(case):
+    from oracle.oracle import LayerConfig
+
+    grid, num, shifted, heads, head_dim, text = case
+    return LayerConfig(*grid, *num, text_tokens=text, shifted=int(shifted), rope_dim=6 * (head_dim // 6) if
+                       head_dim < 126 else 126, heads=heads, head_dim=head_dim)
+
+
+def _inputs(cfg):
+    rng = np.random.default_rng(11)
+    v = rng.standard_normal((cfg.source_tokens, 3, cfg.heads, cfg.head_dim), dtype=np.float32)
+    t = rng.standard_normal((cfg.text_tokens, 3, cfg.heads, cfg.head_dim), dtype=np.float32)
+    return v, t
+
+
+def _rank_main(rank: int, world: int, port: int, case, result_dir: str):
+    import torch
+    import torch.distributed as dist
+
+    import awa_b200
+    from oracle.oracle import Oracle
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = _config(case)
+        oracle = Oracle()
+        v, t = _inputs(cfg)
+        h, d, text = cfg.heads, cfg.head_dim, cfg.text_tokens
+        plan = awa_b200.AwaPlan(*cfg.params[:6], text_tokens=text, shifted=bool(cfg.shifted), rope_dim=cfg.rope_dim,
+                                host_only=True)
+        bounds = plan.partition(world)
+        begin, end = bounds[rank], bounds[rank + 1]
+        W = plan.info.window_count
+        # this rank's windows, as awa_forward_windows computes them
+        maps = oracle.index_maps(cfg)
+        seq = maps["sequence_index"]
+        cu = maps["cu_seqlens"].astype(np.int32)
+        packed = v.reshape(cfg.source_tokens, -1)[np.minimum(seq, cfg.source_tokens - 1)].reshape(-1, 3, h, d).copy()
+        is_text = seq >= cfg.source_tokens
+        packed[is_text] = t[seq[is_text] - cfg.source_tokens]
+        roped = oracle.rope(packed, oracle.rope_table(cfg), h, d, cfg.rope_dim)
+        attended = np.zeros((len(seq), h, d), np.float32)
+        if end > begin:
+            oracle.attention_range(roped, cu, begin, end, h, d, attended)
+        video = np.zeros((cfg.source_tokens, h, d), np.float32)
+        owned = np.zeros(cfg.source_tokens, np.int32)
+        partial = np.zeros((text, h, d), np.float32)
+        for w in range(begin, end):
+            rows = np.arange(cu[w], cu[w + 1] - text)
+            video[seq[rows]] = attended[rows]
+            owned[seq[rows]] += 1
+            partial += attended[cu[w + 1] - text:cu[w + 1]]  # window order, fp32
+        assert int(owned.sum()) == plan.range_video_rows(begin, end)
+        # the exchange: all-reduce of the partials, all-gather of the video rows
+        total = torch.from_numpy(partial)
+        dist.all_reduce(total, op=dist.ReduceOp.SUM)
+        text_out = (total / np.float32(W)).numpy()
+        gathered = [torch.zeros(cfg.source_tokens, h, d) for _ in range(world)]
+        owners = [torch.zeros(cfg.source_tokens, dtype=torch.int32) for _ in range(world)]
+        dist.all_gather(gathered, torch.from_numpy(video))
+        dist.all_gather(owners, torch.from_numpy(owned))
+        if rank == 0:
+            count = sum(o.numpy() for o in owners)
+            merged = sum(g.numpy() for g in gathered)
+            np.savez(os.path.join(result_dir, "result.npz"), video=merged, text=text_out, count=count,
+                     bounds=np.array(bounds))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "x".join(map(str, c[0])) + ("s" if c[2] else ""))
+def test_window_sharded_protocol_matches_single_process(case, tmp_path, oracle):
+    import torch.multiprocessing as mp
+
+    world = 2
+    mp.spawn(_rank_main, args=(world, _free_port(), case, str(tmp_path)), nprocs=world, join=True)
+    res = np.load(tmp_path / "result.npz")
+    cfg = _config(case)
+    v, t = _inputs(cfg)
+    ref = oracle.chain(cfg, v, t)
+    bounds = res["bounds"]
+    assert bounds[0] == 0 and bounds[-1] == len(ref["maps"]["windows"]) and np.all(np.diff(bounds) > 0)
+    assert np.all(res["count"] == 1), "every video token must be computed by exactly one rank"
+    assert np.array_equal(res["video"], ref["video"])
+    assert rel_l2(res["text"], ref["text"]) <= FP32_REL_L2
