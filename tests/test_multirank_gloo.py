@@ -23,7 +23,7 @@ from awa_testlib import FP32_REL_L2, rel_l2
 
 CASES = [
     # grid, window counts, shifted, heads, head_dim, text tokens
-    ((2, 16, 16), (1, 2, 2), True, 2, 16, 6),
+    ((2, 45, 80), (1, 3, 4), True, 2, 16, 6),
     ((3, 12, 20), (2, 3, 4), False, 2, 32, 5),
 ]
 
