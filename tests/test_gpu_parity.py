@@ -42,6 +42,9 @@ CASES = [
     LayerConfig(1, 45, 80, 1, 45, 80, text_tokens=3, shifted=1, heads=1, head_dim=128),
     # a single window holding a single video token
     LayerConfig(1, 1, 1, 1, 1, 1, text_tokens=2, shifted=0, heads=1, head_dim=128),
+    # odd head count with 5 key blocks per window (two query tiles + an odd last
+    # tile): head pairs (0, 1) and a lone head 2 on both kinds of work item
+    LayerConfig(4, 16, 16, 1, 2, 2, shifted=1, heads=3, head_dim=128),
 ]
 
 
