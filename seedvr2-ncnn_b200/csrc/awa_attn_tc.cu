@@ -122,24 +122,55 @@ struct Job
     bool has_b;   // second query tile exists
 };
 
-// The global-memory part of a job (its work item and window). Every role
-// fetches the next job's while it works on the current one: the two dependent
-// loads cost about a microsecond, which would otherwise stall each role at
-// every job boundary.
+// The global-memory part of a job (its work item and window).
 struct JobSource
 {
     int2 item;
     WindowDesc win;
 };
 
+__device__ __forceinline__ int2 fetch_item(const AttnArgs& a, int j, int njobs)
+{
+    return a.items[j < njobs ? j / a.heads : 0];
+}
+
+// One stage (the softmax warps: their job starts with a wait for the first
+// scores anyway, and they have no registers to spare).
 __device__ __forceinline__ JobSource fetch_job(const AttnArgs& a, int j, int njobs)
 {
     JobSource src;
-    const int i = j < njobs ? j / a.heads : 0;
-    src.item = a.items[i];
+    src.item = fetch_item(a, j, njobs);
     src.win = a.plan.windows[src.item.x];
     return src;
 }
+
+// The TMA, RoPE and MMA warps fetch job sources ahead in two stages, so that
+// no load waits on another: the work item two jobs ahead and the window of
+// the next job (whose item arrived a job earlier). A window load issued right
+// after its item load stalls the role for a global-memory latency (about a
+// microsecond) at every job boundary.
+struct JobPrefetch
+{
+    JobSource next;  // job j + gridDim.x
+    int2 item2;      // job j + 2 gridDim.x
+
+    __device__ __forceinline__ JobPrefetch(const AttnArgs& a, int njobs)
+    {
+        next.item = fetch_item(a, blockIdx.x, njobs);
+        next.win = a.plan.windows[next.item.x];
+        item2 = fetch_item(a, blockIdx.x + gridDim.x, njobs);
+    }
+
+    // The source of job j (= the previous `next`); fetches ahead for j + gridDim.x.
+    __device__ __forceinline__ JobSource advance(const AttnArgs& a, int j, int njobs)
+    {
+        const JobSource cur = next;
+        next.item = item2;
+        next.win = a.plan.windows[item2.x];
+        item2 = fetch_item(a, j + 2 * gridDim.x, njobs);
+        return cur;
+    }
+};
 
 template <bool PACKED>
 __device__ __forceinline__ Job decode_job(const AttnArgs& a, int j, const JobSource& src)
@@ -526,11 +557,10 @@ __device__ void tma_role(const AttnArgs& a, const TmaMaps& maps, TcShared& sh, i
     uint32_t q_issued = 0;      // Q loads issued so far
     uint32_t g = 0;             // K/V blocks issued so far
     bool ok = true;
-    JobSource next = fetch_job(a, blockIdx.x, njobs);
+    JobPrefetch pre(a, njobs);
     for (int j = blockIdx.x; j < njobs && ok; j += gridDim.x)
     {
-        const Job job = decode_job<PACKED>(a, j, next);
-        next = fetch_job(a, j + gridDim.x, njobs);
+        const Job job = decode_job<PACKED>(a, j, pre.advance(a, j, njobs));
         // ---- the job's Q tiles (up to 4 blocks) into the staging area
         if (!warp_all(wait_bar(&sh.bar.q_free, q_free_phase, abort, a.error_flag, 41)))
             break;
@@ -611,11 +641,10 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
     // block, and its K row)
     const int row_h = (ptid & 63) / bwc, row_w = (ptid & 63) % bwc;
 
-    JobSource next = fetch_job(a, blockIdx.x, njobs);
+    JobPrefetch pre(a, njobs);
     for (int j = blockIdx.x; j < njobs; j += gridDim.x)
     {
-        const Job job = decode_job<PACKED>(a, j, next);
-        next = fetch_job(a, j + gridDim.x, njobs);
+        const Job job = decode_job<PACKED>(a, j, pre.advance(a, j, njobs));
         const int hoff = job.win.h0 - job.win.h0n, woff = job.win.w0 - job.win.w0n;
         // ---- Q: staging -> (rotate) -> TMEM
         if (!rope_all(wait_bar(&sh.bar.q_loaded, q_loaded_phase, abort, a.error_flag, 11)))
@@ -715,11 +744,10 @@ __device__ void mma_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t tm
     const uint32_t tmem_s[2] = {tmem + kColS, tmem + kColS + 64};
     const uint32_t tmem_o[2] = {tmem + kColO, tmem + kColO + 128};
     bool ok = true;
-    JobSource next = fetch_job(a, blockIdx.x, njobs);
+    JobPrefetch pre(a, njobs);
     for (int j = blockIdx.x; j < njobs && ok; j += gridDim.x)
     {
-        const Job job = decode_job<PACKED>(a, j, next);
-        next = fetch_job(a, j + gridDim.x, njobs);
+        const Job job = decode_job<PACKED>(a, j, pre.advance(a, j, njobs));
         const int slots = job.has_b ? 2 : 1;
         if (!warp_all(wait_bar(&sh.bar.q_full, q_full_phase, abort, a.error_flag, 21)))
             break;
