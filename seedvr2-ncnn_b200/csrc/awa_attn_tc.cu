@@ -806,15 +806,19 @@ __device__ void mma_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t tm
                 if (leader)
                 {
                     issue_pv(tmem_o[s], tmem_s[s], v_addr, n, kb > 0);
-                    tc::mma_commit(&sh.bar.o_full[s]);
                     if (more)
                     {
                         // S of the next block overwrites P of this one: tcgen05.mma
-                        // operations of one thread execute in issue order.
+                        // operations of one thread execute in issue order. The
+                        // commit covers this P V too (a commit tracks every MMA the
+                        // thread issued before it): the softmax may scale O once
+                        // the next scores are in.
                         issue_qk(tmem_s[s], tmem_q[s], tc::smem_addr(sh.kv[(gk + 1) % kStages][0]),
                                  block_n<PACKED>(a, job, kb + 1));
                         tc::mma_commit(&sh.bar.s_full[s]);
                     }
+                    else
+                        tc::mma_commit(&sh.bar.o_full[s]);  // the job's O is complete
                 }
                 __syncwarp();
             }
@@ -851,7 +855,7 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
     const int text = a.plan.text_tokens;
     volatile int* abort = &sh.abort;
     uint32_t s_phase = 0;
-    uint32_t pv_count = 0;  // PV MMAs of this slot issued so far (o_full completions)
+    uint32_t o_phase = 0;   // o_full completes once per job of this slot
     JobSource next = fetch_job(a, blockIdx.x, njobs);
     for (int j = blockIdx.x; j < njobs; j += gridDim.x)
     {
@@ -931,10 +935,8 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
             }
             if (__any_sync(0xffffffffu, rescale))
             {
-                // O of the previous block must be complete before it is scaled.
-                if (!warp_all(wait_bar(&sh.bar.o_full[slot], (pv_count - 1) & 1, abort, a.error_flag, 32)))
-                    return;
-                tc::fence_after_sync();
+                // O holds P V of the blocks before this one, complete: the MMA warp
+                // committed these scores after issuing the previous block's P V.
                 // 16 columns at a time: the 64 scores stay in registers meanwhile
 #pragma unroll 1
                 for (int cc = 0; cc < 8; cc++)
@@ -971,11 +973,11 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
             tc::tmem_wait_st();
             tc::fence_before_sync();
             mbar_arrive(&sh.bar.p_full[slot]);
-            pv_count++;
         }
         // epilogue: wait for the last PV, normalise, store
-        if (!warp_all(wait_bar(&sh.bar.o_full[slot], (pv_count - 1) & 1, abort, a.error_flag, 33)))
+        if (!warp_all(wait_bar(&sh.bar.o_full[slot], o_phase, abort, a.error_flag, 33)))
             return;
+        o_phase ^= 1;
         tc::fence_after_sync();
         const float inv = 1.f / l_run;
 #pragma unroll
