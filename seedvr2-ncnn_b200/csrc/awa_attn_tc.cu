@@ -828,7 +828,8 @@ __device__ void mma_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t tm
             {
                 if (kb + 2 == job.blocks)
                     tc::mma_commit(&sh.bar.q_empty);  // last S MMAs of the job issued: Q TMEM free when done
-                tc::mma_commit(&sh.bar.kv_empty[gk % kStages]);
+                // (the stage of this block is released by the softmax warps of
+                // the job's last slot, which see every MMA that read it complete)
             }
             __syncwarp();
         }
@@ -856,13 +857,20 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
     volatile int* abort = &sh.abort;
     uint32_t s_phase = 0;
     uint32_t o_phase = 0;   // o_full completes once per job of this slot
+    uint32_t g = 0;         // K/V blocks of the jobs before this one
     JobSource next = fetch_job(a, blockIdx.x, njobs);
     for (int j = blockIdx.x; j < njobs; j += gridDim.x)
     {
         const Job job = decode_job<PACKED>(a, j, next);
         next = fetch_job(a, j + gridDim.x, njobs);
+        g += job.blocks;
         if (slot == 1 && !job.has_b)
             continue;
+        // The slot whose MMAs the MMA warp issues last in each block (B if the
+        // job has it) hands the ring stages back to the TMA warp: its commit
+        // after the next block's scores covers every MMA that read this block.
+        // One thread of it arrives; g - blocks is the job's first ring entry.
+        const bool releases = slot == (int)job.has_b && r == 0;
         // this thread's query row: row i of block qb
         const int qb = 2 * (job.qa + slot) + (r >> 6);
         const int qi = r & 63;
@@ -902,6 +910,8 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
                 return;
             s_phase ^= 1;
             tc::fence_after_sync();
+            if (releases && kb > 0)
+                mbar_arrive(&sh.bar.kv_empty[(g - job.blocks + kb - 1) % kStages]);
             uint32_t v[64];
             tc::tmem_ld32(t_s, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
             tc::tmem_ld32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
@@ -978,6 +988,8 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
         if (!warp_all(wait_bar(&sh.bar.o_full[slot], o_phase, abort, a.error_flag, 33)))
             return;
         o_phase ^= 1;
+        if (releases)
+            mbar_arrive(&sh.bar.kv_empty[(g - 1) % kStages]);
         tc::fence_after_sync();
         const float inv = 1.f / l_run;
 #pragma unroll
