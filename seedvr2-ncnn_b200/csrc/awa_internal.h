@@ -101,10 +101,12 @@ int launch_mmrope(const PlanDevice& plan, int heads, int head_dim, int in_dtype,
                   int out_dtype, void* out, int64_t ots, cudaStream_t stream);
 int launch_unpack_video(const PlanDevice& plan, int heads, int head_dim, int in_dtype, const void* attended,
                         int64_t its, int out_dtype, void* video, int64_t vts, cudaStream_t stream);
-// text_out[i] = sum_w src(w, i) / divisor in window order; src(w, i) is either
-// packed row cu[w+1]-text+i of `attended` (packed != 0) or row (w*text+i) of a
-// dense fp32 [W][text][H*d] array. If divisor == 0 the sum is not divided and
-// the result is written as fp32 (partial sums).
+// text_out[i] = mean over windows of src(w, i); src(w, i) is either packed row
+// cu[w+1]-text+i of `attended` (packed != 0: the sum of src / divisor term by
+// term in window order, as the reference's Unpack) or row (w*text+i) of a
+// dense fp32 [W][text][H*d] array (the sum in window order, then / divisor).
+// If divisor == 0 the sum is not divided and the result is written as fp32
+// (partial sums).
 int launch_text_reduce(const PlanDevice& plan, int heads, int head_dim, int packed, int in_dtype, const void* src,
                        int64_t src_token_stride, int window_begin, int window_end, float divisor, int out_dtype,
                        void* text_out, int64_t text_token_stride, cudaStream_t stream);
