@@ -10,7 +10,9 @@ over one synthetic batch of the workload's shape, inputs resident in HBM.
 * value      windows of all ranks / max-over-ranks device time (CUDA events)
 * e2e        same metric through the C ABI with host buffers: pinned-host ->
              device copy of the step's QKV, the forward, device -> host copy of
-             the outputs, every step inside the timed region
+             the outputs, every step inside the timed region; steps pipelined
+             over two device buffer sets (copy in of the next step and copy out
+             of the previous one overlap the forward and each other)
 * roofline   the dominant kernel (fused tcgen05 attention), timed live by the
              library's launch profiler (events on its own stream)
 * cpu_baseline  the reference's own awa_layers.cpp CPU forward (oracle/_ref),
@@ -277,24 +279,53 @@ def run_b200(args, rank, world, local_rank):
     host_t.copy_(text_qkv)
     out_v = torch.empty(video_out.shape, dtype=dtype, pin_memory=True)
     out_t = torch.empty(text_out.shape, dtype=dtype, pin_memory=True)
-    dev_v = torch.empty_like(video_qkv)
-    dev_t = torch.empty_like(text_qkv)
+    # Steps are pipelined as a stream of layers would be: two device buffer
+    # sets; the host->device copy of step i + 1 (copy stream) runs while step i
+    # computes and while the device->host copy of step i - 1 (a second copy
+    # stream; PCIe is full duplex) drains. Every step still copies its whole
+    # input in and its whole output out inside the timed region.
+    dev_in = [(torch.empty_like(video_qkv), torch.empty_like(text_qkv)) for _ in range(2)]
+    dev_out = [(torch.empty_like(video_out), torch.empty_like(text_out)) for _ in range(2)]
+    h2d_stream, d2h_stream = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    in_free, out_free = [None, None], [None, None]  # events: last reader of buffer set b done
 
-    def e2e_step():
-        dev_v.copy_(host_v, non_blocking=True)
-        dev_t.copy_(host_t, non_blocking=True)
-        plan.forward(dev_v, dev_t, prec, out_dtype=dtype, workspace=workspace, video_out=video_out,
-                     text_out=text_out, stream=stream)
-        out_v.copy_(video_out, non_blocking=True)
-        out_t.copy_(text_out, non_blocking=True)
+    def e2e_step(i):
+        b = i % 2
+        dv, dt = dev_in[b]
+        ov, ot = dev_out[b]
+        with torch.cuda.stream(h2d_stream):
+            if in_free[b] is not None:
+                h2d_stream.wait_event(in_free[b])
+            dv.copy_(host_v, non_blocking=True)
+            dt.copy_(host_t, non_blocking=True)
+            loaded = torch.cuda.Event()
+            loaded.record(h2d_stream)
+        stream.wait_event(loaded)
+        if out_free[b] is not None:
+            stream.wait_event(out_free[b])
+        plan.forward(dv, dt, prec, out_dtype=dtype, workspace=workspace, video_out=ov, text_out=ot, stream=stream)
+        computed = torch.cuda.Event()
+        computed.record(stream)
+        in_free[b] = computed
+        with torch.cuda.stream(d2h_stream):
+            d2h_stream.wait_event(computed)
+            out_v.copy_(ov, non_blocking=True)
+            out_t.copy_(ot, non_blocking=True)
+            drained = torch.cuda.Event()
+            drained.record(d2h_stream)
+            out_free[b] = drained
 
-    e2e_step()
+    for i in range(2):
+        e2e_step(i)
     torch.cuda.synchronize()
     barrier()
     e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
+    h2d_stream.wait_event(e_start)
+    d2h_stream.wait_event(e_start)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    stream.wait_event(out_free[(e2e_steps - 1) % 2])
     e_stop.record(stream)
     torch.cuda.synchronize()
     barrier()

@@ -274,55 +274,50 @@ __global__ void text_reduce(PlanDevice plan, int head_row, int packed, const TIn
 }
 
 // text_reduce for dense fp32 partials ([W][text][head_row] rows) whose rows
-// and base are 16-byte aligned: four consecutive elements per thread, 16-byte
-// loads, sixteen windows in flight; the sum in window order, then / divisor
-// (as text_reduce does for dense partials).
+// and base are 8-byte aligned: two consecutive elements per thread, 8-byte
+// loads, sixteen windows in flight per thread (more threads in flight than
+// with 16-byte loads, which measured slower); the sum in window order, then
+// / divisor (as text_reduce does for dense partials).
 template <typename TOut>
-__global__ void text_reduce_v4(int text, int head_row, const float* __restrict__ src, int64_t sts, int windows,
+__global__ void text_reduce_v2(int text, int head_row, const float* __restrict__ src, int64_t sts, int windows,
                                float divisor, TOut* __restrict__ out, int64_t ots)
 {
-    const int quads = head_row >> 2;
-    const int64_t total = (int64_t)text * quads;
+    const int pairs = head_row >> 1;
+    const int64_t total = (int64_t)text * pairs;
     const int64_t step = (int64_t)gridDim.x * blockDim.x;
     for (int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; id < total; id += step)
     {
-        const int i = (int)(id / quads);
-        const int e = (int)(id - (int64_t)i * quads) * 4;
+        const int i = (int)(id / pairs);
+        const int e = (int)(id - (int64_t)i * pairs) * 2;
         const float* col = src + (int64_t)i * sts + e;
         const int64_t wstride = (int64_t)text * sts;  // one window's text rows
         constexpr int kBatch = 16;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        auto add = [&](const float4 x) {
+        float2 acc = make_float2(0.f, 0.f);
+        auto add = [&](const float2 x) {
             acc.x = __fadd_rn(acc.x, x.x);
             acc.y = __fadd_rn(acc.y, x.y);
-            acc.z = __fadd_rn(acc.z, x.z);
-            acc.w = __fadd_rn(acc.w, x.w);
         };
         int w = 0;
         for (; w + kBatch <= windows; w += kBatch)
         {
-            float4 x[kBatch];
+            float2 x[kBatch];
 #pragma unroll
             for (int u = 0; u < kBatch; u++)
-                x[u] = __ldcs(reinterpret_cast<const float4*>(col + (int64_t)(w + u) * wstride));
+                x[u] = __ldcs(reinterpret_cast<const float2*>(col + (int64_t)(w + u) * wstride));
 #pragma unroll
             for (int u = 0; u < kBatch; u++)
                 add(x[u]);
         }
         for (; w < windows; w++)
-            add(__ldcs(reinterpret_cast<const float4*>(col + (int64_t)w * wstride)));
+            add(__ldcs(reinterpret_cast<const float2*>(col + (int64_t)w * wstride)));
         if (divisor != 0.f)
         {
             acc.x = __fdiv_rn(acc.x, divisor);
             acc.y = __fdiv_rn(acc.y, divisor);
-            acc.z = __fdiv_rn(acc.z, divisor);
-            acc.w = __fdiv_rn(acc.w, divisor);
         }
         TOut* o = out + (int64_t)i * ots + e;
         store1(o, acc.x);
         store1(o + 1, acc.y);
-        store1(o + 2, acc.z);
-        store1(o + 3, acc.w);
     }
 }
 
@@ -455,11 +450,11 @@ struct TextReduceLaunch
     {
         const int head_row = heads * head_dim;
         const int threads = 256;
-        if (std::is_same<TIn, float>::value && !packed && head_row % 4 == 0 && sts % 4 == 0 &&
-            reinterpret_cast<uintptr_t>(src) % 16 == 0)
+        if (std::is_same<TIn, float>::value && !packed && head_row % 2 == 0 && sts % 2 == 0 &&
+            reinterpret_cast<uintptr_t>(src) % 8 == 0)
         {
-            const int64_t quads = (int64_t)plan.text_tokens * (head_row / 4);
-            text_reduce_v4<TOut><<<grid_for(quads, threads), threads, 0, stream>>>(
+            const int64_t pairs = (int64_t)plan.text_tokens * (head_row / 2);
+            text_reduce_v2<TOut><<<grid_for(pairs, threads), threads, 0, stream>>>(
                 plan.text_tokens, head_row, (const float*)src, sts, window_end - window_begin, divisor, (TOut*)out,
                 ots);
             return (int)cudaGetLastError();
