@@ -271,68 +271,71 @@ def run_b200(args, rank, world, local_rank):
     value = W * world / (ms_per_step / 1000.0)
     launches = sum(v[0] for v in prof.values())
 
-    # ---- end to end through the C ABI with host buffers
-    e2e_steps = max(3, min(args.steps, args.e2e_steps))
-    host_v = torch.empty(video_qkv.shape, dtype=dtype, pin_memory=True)
-    host_t = torch.empty(text_qkv.shape, dtype=dtype, pin_memory=True)
-    host_v.copy_(video_qkv)
-    host_t.copy_(text_qkv)
-    out_v = torch.empty(video_out.shape, dtype=dtype, pin_memory=True)
-    out_t = torch.empty(text_out.shape, dtype=dtype, pin_memory=True)
-    # Steps are pipelined as a stream of layers would be: two device buffer
-    # sets; the host->device copy of step i + 1 (copy stream) runs while step i
-    # computes and while the device->host copy of step i - 1 (a second copy
-    # stream; PCIe is full duplex) drains. Every step still copies its whole
-    # input in and its whole output out inside the timed region.
-    dev_in = [(torch.empty_like(video_qkv), torch.empty_like(text_qkv)) for _ in range(2)]
-    dev_out = [(torch.empty_like(video_out), torch.empty_like(text_out)) for _ in range(2)]
-    h2d_stream, d2h_stream = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    in_free, out_free = [None, None], [None, None]  # events: last reader of buffer set b done
+    # ---- end to end through the C ABI with host buffers (skipped by --no-e2e,
+    # for profiler captures that should hold little device memory)
+    e2e_ms, e2e_steps = None, 0
+    if not args.no_e2e:
+        e2e_steps = max(3, min(args.steps, args.e2e_steps))
+        host_v = torch.empty(video_qkv.shape, dtype=dtype, pin_memory=True)
+        host_t = torch.empty(text_qkv.shape, dtype=dtype, pin_memory=True)
+        host_v.copy_(video_qkv)
+        host_t.copy_(text_qkv)
+        out_v = torch.empty(video_out.shape, dtype=dtype, pin_memory=True)
+        out_t = torch.empty(text_out.shape, dtype=dtype, pin_memory=True)
+        # Steps are pipelined as a stream of layers would be: two device buffer
+        # sets; the host->device copy of step i + 1 (copy stream) runs while step i
+        # computes and while the device->host copy of step i - 1 (a second copy
+        # stream; PCIe is full duplex) drains. Every step still copies its whole
+        # input in and its whole output out inside the timed region.
+        dev_in = [(torch.empty_like(video_qkv), torch.empty_like(text_qkv)) for _ in range(2)]
+        dev_out = [(torch.empty_like(video_out), torch.empty_like(text_out)) for _ in range(2)]
+        h2d_stream, d2h_stream = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        in_free, out_free = [None, None], [None, None]  # events: last reader of buffer set b done
 
-    def e2e_step(i):
-        b = i % 2
-        dv, dt = dev_in[b]
-        ov, ot = dev_out[b]
-        with torch.cuda.stream(h2d_stream):
-            if in_free[b] is not None:
-                h2d_stream.wait_event(in_free[b])
-            dv.copy_(host_v, non_blocking=True)
-            dt.copy_(host_t, non_blocking=True)
-            loaded = torch.cuda.Event()
-            loaded.record(h2d_stream)
-        stream.wait_event(loaded)
-        if out_free[b] is not None:
-            stream.wait_event(out_free[b])
-        plan.forward(dv, dt, prec, out_dtype=dtype, workspace=workspace, video_out=ov, text_out=ot, stream=stream)
-        computed = torch.cuda.Event()
-        computed.record(stream)
-        in_free[b] = computed
-        with torch.cuda.stream(d2h_stream):
-            d2h_stream.wait_event(computed)
-            out_v.copy_(ov, non_blocking=True)
-            out_t.copy_(ot, non_blocking=True)
-            drained = torch.cuda.Event()
-            drained.record(d2h_stream)
-            out_free[b] = drained
+        def e2e_step(i):
+            b = i % 2
+            dv, dt = dev_in[b]
+            ov, ot = dev_out[b]
+            with torch.cuda.stream(h2d_stream):
+                if in_free[b] is not None:
+                    h2d_stream.wait_event(in_free[b])
+                dv.copy_(host_v, non_blocking=True)
+                dt.copy_(host_t, non_blocking=True)
+                loaded = torch.cuda.Event()
+                loaded.record(h2d_stream)
+            stream.wait_event(loaded)
+            if out_free[b] is not None:
+                stream.wait_event(out_free[b])
+            plan.forward(dv, dt, prec, out_dtype=dtype, workspace=workspace, video_out=ov, text_out=ot, stream=stream)
+            computed = torch.cuda.Event()
+            computed.record(stream)
+            in_free[b] = computed
+            with torch.cuda.stream(d2h_stream):
+                d2h_stream.wait_event(computed)
+                out_v.copy_(ov, non_blocking=True)
+                out_t.copy_(ot, non_blocking=True)
+                drained = torch.cuda.Event()
+                drained.record(d2h_stream)
+                out_free[b] = drained
 
-    for i in range(2):
-        e2e_step(i)
-    torch.cuda.synchronize()
-    barrier()
-    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record(stream)
-    h2d_stream.wait_event(e_start)
-    d2h_stream.wait_event(e_start)
-    for i in range(e2e_steps):
-        e2e_step(i)
-    stream.wait_event(out_free[(e2e_steps - 1) % 2])
-    e_stop.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    te = torch.tensor([e_start.elapsed_time(e_stop)], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = float(te.item()) / e2e_steps
+        for i in range(2):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        barrier()
+        e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        h2d_stream.wait_event(e_start)
+        d2h_stream.wait_event(e_start)
+        for i in range(e2e_steps):
+            e2e_step(i)
+        stream.wait_event(out_free[(e2e_steps - 1) % 2])
+        e_stop.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        te = torch.tensor([e_start.elapsed_time(e_stop)], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = float(te.item()) / e2e_steps
     clock = clocks.stop()
     awa_b200.device_status()
 
@@ -385,9 +388,9 @@ def run_b200(args, rank, world, local_rank):
                        "parallelism": f"weak: {world} independent layer(s), one per GPU"},
             "attn_tflops": round(flops * world / (ms_per_step / 1000.0) / 1e12, 2),
             "gpu_launches": launches,
-            "e2e": {"value": round(W * world / (e2e_ms / 1000.0), 2), "unit": UNIT,
-                    "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes, "steps": e2e_steps,
-                    "ms_per_step": round(e2e_ms, 4)},
+            "e2e": None if e2e_ms is None else {
+                "value": round(W * world / (e2e_ms / 1000.0), 2), "unit": UNIT, "h2d_bytes_per_step": in_bytes,
+                "d2h_bytes_per_step": out_bytes, "steps": e2e_steps, "ms_per_step": round(e2e_ms, 4)},
             "roofline": roofline,
             "clocks": clock,
             "profile": {k: {"launches": v[0], "ms": round(v[1], 4)} for k, v in prof.items()},
@@ -404,6 +407,7 @@ def main():
     parser.add_argument("--workload", default="cfg4", choices=sorted(WORKLOADS))
     parser.add_argument("--e2e-steps", type=int, default=20)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiler captures)")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
