@@ -40,7 +40,7 @@
 //   warps 4-7   query row; online max (O rescaled only when the max grows by
 //               more than 2^8), exp2, P rounded to bf16 and written over S in
 //               TMEM; at the end O / l is stored (video rows to source order,
-//               text rows to the fp32 partials).
+//               text rows to the bf16 per-window partials).
 //
 // TMEM (512 columns): Q_A 0-63, Q_B 64-127, S_A 128-191, S_B 192-255,
 // O_A 256-383, O_B 384-511. Hand-offs are mbarriers (TMA transaction counts,
@@ -1001,10 +1001,12 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
             tc::tmem_wait_ld();
             if (dst >= 0)
             {
-                // this thread's row: 64 fp32 (text partials, fp32 out) or bf16 values
-                const bool f32 = (!PACKED && text_row) || sizeof(TOut) == 4;
-                char* row = (!PACKED && text_row) ? reinterpret_cast<char*>(a.text_partial + dst + h * 64)
-                                                  : static_cast<char*>(a.out) + (dst + h * 64) * (int64_t)sizeof(TOut);
+                // this thread's row: 64 fp32 (fp32 out) or bf16 values (bf16 out, and
+                // the text partials, as the layer chain's bf16 attended rows)
+                const bool f32 = !(!PACKED && text_row) && sizeof(TOut) == 4;
+                char* row = (!PACKED && text_row)
+                                ? reinterpret_cast<char*>(reinterpret_cast<bf16*>(a.text_partial) + dst + h * 64)
+                                : static_cast<char*>(a.out) + (dst + h * 64) * (int64_t)sizeof(TOut);
                 if (f32)
                 {
 #pragma unroll
@@ -1264,7 +1266,7 @@ int launch_attention_tc(const AttnArgs& args, int packed, int in_dtype, int out_
     AttnArgs a = args;
     const int64_t out_size = out_dtype == kF32 ? 4 : 2;
     a.out_v8 = (reinterpret_cast<uintptr_t>(args.out) % 32 == 0) && (args.out_token_stride * out_size) % 32 == 0 &&
-               (reinterpret_cast<uintptr_t>(args.text_partial) % 32 == 0) && (args.heads * args.head_dim * 4) % 32 == 0;
+               (reinterpret_cast<uintptr_t>(args.text_partial) % 32 == 0) && (args.heads * args.head_dim * 2) % 32 == 0;
     ProfileScope prof(packed ? "awa_attention_tc_packed" : "awa_attention_tc_fused", stream);
     // The packed path applies no RoPE; the fused path has a 126-wide (21 pairs per axis) instance.
     const bool rd126 = p.rope_dim == 126 && p.pairs_per_axis == 21;

@@ -11,8 +11,6 @@
 
 #include <cuda_bf16.h>
 
-#include <type_traits>
-
 namespace awa
 {
 namespace
@@ -273,13 +271,25 @@ __global__ void text_reduce(PlanDevice plan, int head_row, int packed, const TIn
     }
 }
 
-// text_reduce for dense fp32 partials ([W][text][head_row] rows) whose rows
-// and base are 8-byte aligned: two consecutive elements per thread, 8-byte
-// loads, sixteen windows in flight per thread (more threads in flight than
-// with 16-byte loads, which measured slower); the sum in window order, then
-// / divisor (as text_reduce does for dense partials).
-template <typename TOut>
-__global__ void text_reduce_v2(int text, int head_row, const float* __restrict__ src, int64_t sts, int windows,
+// Two consecutive elements of a dense partial row, streamed (read once).
+__device__ __forceinline__ float2 load_pair_cs(const float* p)
+{
+    return __ldcs(reinterpret_cast<const float2*>(p));
+}
+
+__device__ __forceinline__ float2 load_pair_cs(const __nv_bfloat16* p)
+{
+    const unsigned int w = __ldcs(reinterpret_cast<const unsigned int*>(p));
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+// text_reduce for dense partials ([W][text][head_row] rows of fp32 or bf16)
+// whose rows and base are aligned to two elements: two consecutive elements
+// per thread, sixteen windows in flight per thread (more threads in flight
+// than with 16-byte loads, which measured slower); the sum in window order,
+// then / divisor (as text_reduce does for dense partials).
+template <typename TIn, typename TOut>
+__global__ void text_reduce_v2(int text, int head_row, const TIn* __restrict__ src, int64_t sts, int windows,
                                float divisor, TOut* __restrict__ out, int64_t ots)
 {
     const int pairs = head_row >> 1;
@@ -289,27 +299,30 @@ __global__ void text_reduce_v2(int text, int head_row, const float* __restrict__
     {
         const int i = (int)(id / pairs);
         const int e = (int)(id - (int64_t)i * pairs) * 2;
-        const float* col = src + (int64_t)i * sts + e;
+        const TIn* col = src + (int64_t)i * sts + e;
         const int64_t wstride = (int64_t)text * sts;  // one window's text rows
         constexpr int kBatch = 16;
         float2 acc = make_float2(0.f, 0.f);
-        auto add = [&](const float2 x) {
-            acc.x = __fadd_rn(acc.x, x.x);
-            acc.y = __fadd_rn(acc.y, x.y);
-        };
         int w = 0;
         for (; w + kBatch <= windows; w += kBatch)
         {
             float2 x[kBatch];
 #pragma unroll
             for (int u = 0; u < kBatch; u++)
-                x[u] = __ldcs(reinterpret_cast<const float2*>(col + (int64_t)(w + u) * wstride));
+                x[u] = load_pair_cs(col + (int64_t)(w + u) * wstride);
 #pragma unroll
             for (int u = 0; u < kBatch; u++)
-                add(x[u]);
+            {
+                acc.x = __fadd_rn(acc.x, x[u].x);
+                acc.y = __fadd_rn(acc.y, x[u].y);
+            }
         }
         for (; w < windows; w++)
-            add(__ldcs(reinterpret_cast<const float2*>(col + (int64_t)w * wstride)));
+        {
+            const float2 x = load_pair_cs(col + (int64_t)w * wstride);
+            acc.x = __fadd_rn(acc.x, x.x);
+            acc.y = __fadd_rn(acc.y, x.y);
+        }
         if (divisor != 0.f)
         {
             acc.x = __fdiv_rn(acc.x, divisor);
@@ -450,12 +463,11 @@ struct TextReduceLaunch
     {
         const int head_row = heads * head_dim;
         const int threads = 256;
-        if (std::is_same<TIn, float>::value && !packed && head_row % 2 == 0 && sts % 2 == 0 &&
-            reinterpret_cast<uintptr_t>(src) % 8 == 0)
+        if (!packed && head_row % 2 == 0 && sts % 2 == 0 && reinterpret_cast<uintptr_t>(src) % (2 * sizeof(TIn)) == 0)
         {
             const int64_t pairs = (int64_t)plan.text_tokens * (head_row / 2);
-            text_reduce_v2<TOut><<<grid_for(pairs, threads), threads, 0, stream>>>(
-                plan.text_tokens, head_row, (const float*)src, sts, window_end - window_begin, divisor, (TOut*)out,
+            text_reduce_v2<TIn, TOut><<<grid_for(pairs, threads), threads, 0, stream>>>(
+                plan.text_tokens, head_row, (const TIn*)src, sts, window_end - window_begin, divisor, (TOut*)out,
                 ots);
             return (int)cudaGetLastError();
         }

@@ -83,7 +83,9 @@ struct AttnArgs
     // outputs
     void* out = nullptr;
     int64_t out_token_stride = 0;
-    float* text_partial = nullptr;  // fused: [window - window_begin][text][H][d]
+    // fused: [window - window_begin][text][H][d] text rows of each window, fp32
+    // (SIMT kernel) or bf16 (tcgen05 kernel)
+    float* text_partial = nullptr;
     // work list: (window, q tile) items (SIMT: 64-row tiles; tcgen05: pairs of
     // 128-row tiles), each taken for every head
     const int2* items = nullptr;
@@ -104,7 +106,8 @@ int launch_unpack_video(const PlanDevice& plan, int heads, int head_dim, int in_
 // text_out[i] = mean over windows of src(w, i); src(w, i) is either packed row
 // cu[w+1]-text+i of `attended` (packed != 0: the sum of src / divisor term by
 // term in window order, as the reference's Unpack) or row (w*text+i) of a
-// dense fp32 [W][text][H*d] array (the sum in window order, then / divisor).
+// dense [W][text][H*d] array of in_dtype (the sum in window order, then /
+// divisor).
 // If divisor == 0 the sum is not divided and the result is written as fp32
 // (partial sums).
 int launch_text_reduce(const PlanDevice& plan, int heads, int head_dim, int packed, int in_dtype, const void* src,

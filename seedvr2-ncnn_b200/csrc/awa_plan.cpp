@@ -733,10 +733,15 @@ static const int2* range_items(awa_plan* plan, bool tc, int begin, int end, int*
     return d;
 }
 
+// Runs the fused attention over windows [window_begin, window_end); the text
+// rows' per-window outputs go to the workspace as partials of *partial_dtype
+// (bf16 from the tensor-core kernel, as the layer chain's bf16 attended rows;
+// fp32 from the SIMT kernel).
 static int forward_impl(const awa_plan* cplan, int precision, int heads, int head_dim, int window_begin,
                         int window_end, int in_dtype, const void* video_qkv, int64_t vts, int64_t vqs,
                         const void* text_qkv, int64_t tts, int64_t tqs, int out_dtype, void* video_out,
-                        int64_t vots, void* workspace, size_t workspace_bytes, cudaStream_t stream)
+                        int64_t vots, void* workspace, size_t workspace_bytes, int* partial_dtype,
+                        cudaStream_t stream)
 {
     awa_plan* plan = const_cast<awa_plan*>(cplan);
     const int64_t head_row = (int64_t)heads * head_dim;
@@ -751,6 +756,7 @@ static int forward_impl(const awa_plan* cplan, int precision, int heads, int hea
     if (!workspace || workspace_bytes < need)
         return fail(AWA_ERR_INVALID, "awa_forward: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
     const bool tc = awa_attention_kernel_kind(plan, precision, in_dtype, heads, head_dim) == 1;
+    *partial_dtype = tc ? AWA_BF16 : AWA_F32;
     if (tc)
     {
         const size_t in_size = dtype_size(in_dtype), out_size = dtype_size(out_dtype);
@@ -790,12 +796,13 @@ int awa_forward(const awa_plan* plan, int precision, int heads, int head_dim, in
         return rc;
     if (!text_out || text_token_stride_out < (int64_t)heads * head_dim)
         return fail(AWA_ERR_INVALID, "awa_forward: invalid text output");
+    int partial_dtype = AWA_F32;
     rc = forward_impl(plan, precision, heads, head_dim, 0, plan->info.window_count, in_dtype, video_qkv,
                       video_token_stride, video_qkv_stride, text_qkv, text_token_stride, text_qkv_stride, out_dtype,
-                      video_out, video_token_stride_out, workspace, workspace_bytes, stream);
+                      video_out, video_token_stride_out, workspace, workspace_bytes, &partial_dtype, stream);
     if (rc)
         return rc;
-    return launch_status(awa::launch_text_reduce(plan->dev, heads, head_dim, 0, AWA_F32, workspace,
+    return launch_status(awa::launch_text_reduce(plan->dev, heads, head_dim, 0, partial_dtype, workspace,
                                                  (int64_t)heads * head_dim, 0, plan->info.window_count,
                                                  (float)plan->info.window_count, out_dtype, text_out,
                                                  text_token_stride_out, stream),
@@ -817,13 +824,14 @@ int awa_forward_windows(const awa_plan* plan, int precision, int heads, int head
         return launch_status(cudaMemsetAsync(text_partial, 0,
                                              (size_t)plan->info.text_tokens * heads * head_dim * sizeof(float), stream),
                              "memset text partial");
+    int partial_dtype = AWA_F32;
     rc = forward_impl(plan, precision, heads, head_dim, window_begin, window_end, in_dtype, video_qkv,
                       video_token_stride, video_qkv_stride, text_qkv, text_token_stride, text_qkv_stride, out_dtype,
-                      video_out, video_token_stride_out, workspace, workspace_bytes, stream);
+                      video_out, video_token_stride_out, workspace, workspace_bytes, &partial_dtype, stream);
     if (rc)
         return rc;
     // Unnormalised partial sum over this range, in window order.
-    return launch_status(awa::launch_text_reduce(plan->dev, heads, head_dim, 0, AWA_F32, workspace,
+    return launch_status(awa::launch_text_reduce(plan->dev, heads, head_dim, 0, partial_dtype, workspace,
                                                  (int64_t)heads * head_dim, window_begin, window_end, 0.f, AWA_F32,
                                                  text_partial, (int64_t)heads * head_dim, stream),
                          "awa_forward_windows text partial");
