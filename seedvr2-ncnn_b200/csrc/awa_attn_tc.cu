@@ -69,7 +69,7 @@ constexpr int kKvPanel = kKeys * 128;  // 64 bf16 features x 64 rows (8 KB)
 constexpr int kKvTile = 2 * kKvPanel;  // 64 x 128 bf16 (16 KB)
 constexpr int kQPanel = kQRows * 128;  // 64 features x 128 rows (16 KB)
 constexpr int kQTile = 2 * kQPanel;    // 128 x 128 bf16 (32 KB)
-constexpr int kStages = 4;             // K/V ring depth
+constexpr int kStages = 5;             // K/V ring depth (with the Q staging: 224 KB of shared memory)
 constexpr int kSoftmaxWarps = 8;
 constexpr int kRopeWarp0 = 8;
 constexpr int kMmaWarp = 12;
@@ -79,7 +79,6 @@ constexpr uint32_t kTmemColumns = 512;
 constexpr uint32_t kColQ = 0;    // + 64 * tile
 constexpr uint32_t kColS = 128;  // + 64 * tile
 constexpr uint32_t kColO = 256;  // + 128 * tile
-constexpr int kRopeSmemEntries = 4096;            // (cos, sin) bf16 pairs: 16 KB
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: healthy waits last microseconds
 constexpr uint64_t kDrainLimitNs = 200000000ull;  // 0.2 s for copies / MMAs in flight at exit
 
@@ -104,7 +103,6 @@ struct TcShared
 {
     uint8_t q[2][kQTile];             // Q staging of tiles A, B
     uint8_t kv[kStages][2][kKvTile];  // [stage][K, V]
-    uint32_t rope[kRopeSmemEntries];  // the plan's bf16 (cos, sin) RoPE table
     Barriers bar;
     uint32_t tmem_base;
     int abort;
@@ -447,7 +445,7 @@ __device__ __forceinline__ void rotate_half_row(uint32_t (&words)[32], const int
     {
         const int pair = 32 * HALF + k;  // features 2 pair, 2 pair + 1
         const int b = pair < ppa ? base[0] : pair < 2 * ppa ? base[1] : base[2];
-        cs[k] = table[2 * pair < rope_dim ? b + pair : 0];
+        cs[k] = __ldg(table + (2 * pair < rope_dim ? b + pair : 0));
     }
 #pragma unroll
     for (int k = 0; k < 32; k++)
@@ -632,7 +630,7 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
     const int ppa = RD ? RD / 6 : a.plan.pairs_per_axis;
     const int rope_dim = RD ? RD : a.plan.rope_dim;
     const int bwc = a.plan.tc_bwc > 0 ? a.plan.tc_bwc : 1;
-    const uint32_t* table = sh.rope;
+    const uint32_t* table = a.plan.rope_table_bf16;  // read through L1
     volatile int* abort = &sh.abort;
     uint32_t q_loaded_phase = 0;
     uint32_t q_empty_phase = 1;  // TMEM Q starts free
@@ -1108,13 +1106,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = threadIdx.x; i < n; i += kThreads)
             z[i] = make_uint4(0, 0, 0, 0);
     }
-    if (!PACKED)
-    {
-        // The RoPE table lives in shared memory (launch_attention_tc checks its size).
-        const int rope_entries = a.plan.max_coord * a.plan.pairs_per_axis;
-        for (int i = threadIdx.x; i < rope_entries; i += kThreads)
-            sh.rope[i] = a.plan.rope_table_bf16[i];
-    }
     tc::fence_async_smem();  // the zeros land before any TMA write or MMA read
     tc::fence_before_sync();
     __syncthreads();
@@ -1257,7 +1248,7 @@ int launch_attention_tc(const AttnArgs& args, int packed, int in_dtype, int out_
     if (args.head_dim != kHeadDim || in_dtype != kBF16)
         return (int)cudaErrorInvalidValue;
     if ((long long)args.item_count * args.heads > 0x7fffffffLL ||
-        (long long)p.max_coord * p.pairs_per_axis > kRopeSmemEntries || p.tc_rows <= 0 || p.tc_rows > kKeys ||
+        p.tc_rows <= 0 || p.tc_rows > kKeys ||
         p.text_tokens <= 0)
         return (int)cudaErrorInvalidValue;
     TmaMaps maps;

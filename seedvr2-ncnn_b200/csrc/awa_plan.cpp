@@ -609,12 +609,7 @@ int awa_mmrope(const awa_plan* plan, int heads, int head_dim, int in_dtype, cons
 int awa_attention_kernel_kind(const awa_plan* plan, int precision, int in_dtype, int heads, int head_dim)
 {
     (void)heads;
-    // The tcgen05 kernel keeps the (coordinate, pair) RoPE table in 16 KB of
-    // shared memory: 4096 entries, i.e. window extents up to ~195 at rope_dim 126.
-    const bool table_fits = plan && (long long)plan->max_coord * plan->pairs_per_axis <= 4096;
-    return precision == AWA_PREC_BF16 && in_dtype == AWA_BF16 && head_dim == 128 && table_fits && plan->tc_slabs
-               ? 1
-               : 2;
+    return plan && precision == AWA_PREC_BF16 && in_dtype == AWA_BF16 && head_dim == 128 && plan->tc_slabs ? 1 : 2;
 }
 
 static int run_attention(const awa_plan* plan, int precision, awa::AttnArgs& args, int packed, int in_dtype,

@@ -45,6 +45,8 @@ CASES = [
     # odd head count with 5 key blocks per window (two query tiles + an odd last
     # tile): head pairs (0, 1) and a lone head 2 on both kinds of work item
     LayerConfig(4, 16, 16, 1, 2, 2, shifted=1, heads=3, head_dim=128),
+    # one 8x256 window (2106 rows, 1x64 boxes): a RoPE table of ~6.6K entries
+    LayerConfig(1, 8, 256, 1, 1, 1, shifted=0, heads=2, head_dim=128),
 ]
 
 
