@@ -220,6 +220,27 @@ int64_t awa_window_range_video_rows(const awa_plan* plan, int window_begin, int 
  * attention cost (sum of L^2); bounds receives parts+1 window indices. */
 int awa_partition_windows(const awa_plan* plan, int parts, int* bounds);
 
+/* The producer of the AWA input (the block's QKV projection with the per-head
+ * RMSNorm of Q and K), on the tensor cores. Replaces, for one branch (video or
+ * text) of a DiT block, proj_qkv + norm_q + norm_k of
+ * tools/reference/dit_block.py:280-287 (ncnn: the block's Gemm, DitRMSNorm
+ * src/dit/dit_precision.cpp:22-90 with shader dit_rmsnorm.comp, and
+ * DitQKVConcat :95-142). out[t] = (RMSNorm_q(q heads), RMSNorm_k(k heads),
+ * v heads) of bf16(x[t] W^T), the RMSNorm per head in fp32: y = x *
+ * rsqrt(sum(x^2) / head_dim + eps) * gamma.
+ *   x:   tokens rows of model_dim bf16, x_stride elements apart (16-byte rows)
+ *   w:   the Linear weight as nn.Linear stores it: 3*heads*head_dim rows of
+ *        model_dim bf16 ([out][in]), w_stride elements apart (16-byte rows)
+ *   gamma_q, gamma_k: head_dim fp32 RMSNorm weights (device memory)
+ *   out: tokens rows of 3*heads*head_dim out_dtype (AWA_BF16 or AWA_F32),
+ *        out_stride elements apart (32-byte aligned rows): the rows
+ *        awa_forward reads as video_qkv / text_qkv.
+ * head_dim must be 128. The Q/K rows are rounded to out_dtype after the
+ * RMSNorm (the reference keeps them in fp32 into its fp32 attention). */
+int awa_qkv_project(int tokens, int model_dim, int heads, int head_dim, const void* x, int64_t x_stride,
+                    const void* w, int64_t w_stride, const float* gamma_q, const float* gamma_k, float eps,
+                    int out_dtype, void* out, int64_t out_stride, awa_stream_t stream);
+
 /* Device-side status of the library on the current device: 0, or the code of
  * the first device check that failed since the last call (a bounded wait that
  * gave up). Synchronises the device. Clears the flag. */

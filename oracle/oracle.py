@@ -172,6 +172,37 @@ class Oracle:
         return out
 
 
+def round_bf16_rne(x: np.ndarray) -> np.ndarray:
+    """fp32 -> nearest bf16 (ties to even), returned as fp32 (finite inputs)."""
+    bits = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    rounded = (bits + np.uint32(0x7FFF) + ((bits >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)
+    return rounded.view(np.float32)
+
+
+def qkv_project(x: np.ndarray, w: np.ndarray, gamma_q: np.ndarray, gamma_k: np.ndarray, eps: float, heads: int,
+                head_dim: int = 128) -> np.ndarray:
+    """The producer of the AWA input: a DiT block's QKV projection and the
+    per-head RMSNorm of Q and K (tools/reference/dit_block.py:280-287).
+
+    proj_qkv is a bias-free Linear (dit_block.py:252-253) whose output, in the
+    bf16 blocks, is bf16: x @ w.T accumulated in fp32, rounded to bf16.
+    norm_q / norm_k are nn.RMSNorm(head_dim, eps, affine) (FixedRMSNorm,
+    dit_block.py:157-166), computed as DitRMSNorm does (src/dit/
+    dit_precision.cpp:22-90, shader dit_rmsnorm.comp:23-48): fp32 squares and
+    sum, inversesqrt(sum / head_dim + eps), times gamma; V is left as is.
+    x [tokens, model_dim] and w [3*heads*head_dim, model_dim] hold bf16 values
+    as fp32. Returns [tokens, 3, heads, head_dim] fp32.
+    """
+    acc = np.asarray(x, np.float32) @ np.asarray(w, np.float32).T
+    y = round_bf16_rne(acc).reshape(acc.shape[0], 3, heads, head_dim)
+    for part, gamma in ((0, gamma_q), (1, gamma_k)):
+        v = y[:, part]
+        ss = np.einsum("thd,thd->th", v, v, dtype=np.float32)
+        coef = (np.float32(1) / np.sqrt(ss / np.float32(head_dim) + np.float32(eps))).astype(np.float32)
+        y[:, part] = v * coef[..., None] * np.asarray(gamma, np.float32)
+    return y
+
+
 class Reference:
     """The reference's own awa_layers.cpp CPU forward (oracle/_ref)."""
 

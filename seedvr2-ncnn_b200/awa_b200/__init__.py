@@ -38,7 +38,8 @@ EXPORTED_SYMBOLS = (
     "awa_pack", "awa_mmrope", "awa_window_attention", "awa_unpack", "awa_forward_workspace_bytes", "awa_forward",
     "awa_forward_noalloc",
     "awa_forward_windows", "awa_text_finalize", "awa_scatter_video_shard", "awa_gather_video_shard",
-    "awa_window_range_video_rows", "awa_partition_windows", "awa_device_status", "awa_attention_kernel_kind",
+    "awa_window_range_video_rows", "awa_partition_windows", "awa_qkv_project", "awa_device_status",
+    "awa_attention_kernel_kind",
     "awa_profile_enable", "awa_profile_reset", "awa_profile_collect", "awa_last_error", "awa_version",
 )
 
@@ -94,6 +95,7 @@ def library() -> ctypes.CDLL:
         "awa_forward_workspace_bytes": (sz, [p, i, i]),
         "awa_forward": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p, sz, p]),
         "awa_forward_noalloc": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p]),
+        "awa_qkv_project": (i, [i, i, i, i, p, i64, p, i64, p, p, ctypes.c_float, i, p, i64, p]),
         "awa_forward_windows": (i, [p, i, i, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, p, sz, p]),
         "awa_text_finalize": (i, [p, i, i, p, i, p, i64, p]),
         "awa_scatter_video_shard": (i, [p, i, i, i, i, i, p, p, i64, p]),
@@ -360,6 +362,21 @@ class AwaPlan:
         return int(library().awa_attention_kernel_kind(self._handle, precision, code, heads, head_dim))
 
 
+def qkv_project(x, w, gamma_q, gamma_k, eps: float, heads: int, out_dtype=None, out=None, stream=None):
+    """The block's QKV projection with the per-head RMSNorm of Q and K
+    (awa_qkv_project): x [tokens, model_dim] bf16, w [3*heads*128, model_dim]
+    bf16 (nn.Linear layout), gamma_q / gamma_k [128] fp32 -> [tokens, 3, heads,
+    128] in out_dtype (bf16 by default), the rows awa_forward reads."""
+    torch = _torch()
+    tokens, model_dim = x.shape
+    if out is None:
+        out = torch.empty(tokens, 3, heads, 128, dtype=out_dtype or torch.bfloat16, device=x.device)
+    _check(library().awa_qkv_project(tokens, model_dim, heads, 128, x.data_ptr(), x.stride(0), w.data_ptr(),
+                                     w.stride(0), gamma_q.data_ptr(), gamma_k.data_ptr(), float(eps),
+                                     _dtype_code(out), out.data_ptr(), out.stride(0), _stream_ptr(stream)))
+    return out
+
+
 def device_status() -> None:
     """Raise if a device-side check of the library failed since the last call."""
     _check(library().awa_device_status())
@@ -442,4 +459,4 @@ def ncnn_run_chain(params: Sequence[int], heads: int, head_dim: int, video_qkv, 
 
 
 __all__ = ["AwaPlan", "AwaError", "PlanInfo", "library", "make_windows", "device_status", "ncnn_run_chain",
-           "EXPORTED_SYMBOLS", "AWA_F32", "AWA_BF16", "AWA_PREC_FP32", "AWA_PREC_BF16"]
+           "EXPORTED_SYMBOLS", "qkv_project", "AWA_F32", "AWA_BF16", "AWA_PREC_FP32", "AWA_PREC_BF16"]

@@ -122,6 +122,11 @@ int launch_shard_copy(const PlanDevice& plan, int heads, int head_dim, int windo
 // Attention: packed != 0 selects packed mode. Template dispatch on dtypes.
 int launch_attention_simt(const AttnArgs& args, int packed, int in_dtype, int out_dtype, cudaStream_t stream);
 int launch_attention_tc(const AttnArgs& args, int packed, int in_dtype, int out_dtype, cudaStream_t stream);
+// x W^T with the per-head RMSNorm of Q and K (head_dim 128); arguments checked
+// by the caller.
+int launch_qkv_project(int tokens, int model_dim, int heads, const void* x, int64_t x_stride, const void* w,
+                       int64_t w_stride, const float* gamma_q, const float* gamma_k, float eps, int out_dtype,
+                       void* out, int64_t out_stride, cudaStream_t stream);
 
 int* device_error_flag();  // per-device flag in device memory
 // Sets the calling thread's awa_last_error() text; returns code.

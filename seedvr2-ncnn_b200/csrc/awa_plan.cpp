@@ -846,6 +846,26 @@ int awa_text_finalize(const awa_plan* plan, int heads, int head_dim, const float
                          "awa_text_finalize");
 }
 
+int awa_qkv_project(int tokens, int model_dim, int heads, int head_dim, const void* x, int64_t x_stride,
+                    const void* w, int64_t w_stride, const float* gamma_q, const float* gamma_k, float eps,
+                    int out_dtype, void* out, int64_t out_stride, awa_stream_t stream)
+{
+    if (head_dim != 128)
+        return fail(AWA_ERR_INVALID, "awa_qkv_project: head_dim %d (the tensor-core kernel needs 128)", head_dim);
+    const int64_t n_out = 3 * (int64_t)heads * head_dim;
+    if (tokens <= 0 || model_dim <= 0 || heads <= 0 || n_out > 0x7fffffff || !x || !w || !gamma_q || !gamma_k ||
+        !out || !valid_dtype(out_dtype) || x_stride < model_dim || w_stride < model_dim || out_stride < n_out ||
+        !(eps >= 0.f))
+        return fail(AWA_ERR_INVALID, "awa_qkv_project: invalid sizes, dtype, eps or NULL tensor");
+    const size_t osz = dtype_size(out_dtype);
+    if (!is_aligned16(x) || !is_aligned16(w) || (x_stride * 2) % 16 || (w_stride * 2) % 16 ||
+        reinterpret_cast<uintptr_t>(out) % 32 || (out_stride * (int64_t)osz) % 32)
+        return fail(AWA_ERR_INVALID, "awa_qkv_project: x and w need 16-byte aligned rows, out 32-byte aligned rows");
+    return launch_status(awa::launch_qkv_project(tokens, model_dim, heads, x, x_stride, w, w_stride, gamma_q, gamma_k,
+                                                 eps, out_dtype, out, out_stride, static_cast<cudaStream_t>(stream)),
+                         "awa_qkv_project launch");
+}
+
 int64_t awa_window_range_video_rows(const awa_plan* plan, int window_begin, int window_end)
 {
     if (!plan || window_begin < 0 || window_end > plan->info.window_count || window_begin > window_end)

@@ -15,6 +15,11 @@ HGinkgo/SeedVR2-ncnn and records, for each configuration:
 * ``chain_*.npz``: one seeded forward of AwaAttentionPack -> 3D RoPE
   (dit_block.py:70-96 frequencies, :223-231 rotation, gathered as in :268-278)
   -> AwaWindowAttention -> AwaAttentionUnpack, with its inputs.
+* ``qkv_project.npz``: the producer of the AWA input, run with the modules of
+  FixedMMAttention (dit_block.py:234-263) as its forward does (:280-287): the
+  bf16 proj_qkv Linear, then norm_q / norm_k (FixedRMSNorm) on Q and K.
+
+``--only qkv`` writes just the last one.
 
 The fixtures are small (a few hundred KB) and are what the CPU tests compare the
 C oracle against; the GPU tests never read the reference.
@@ -66,12 +71,47 @@ def sha(array) -> str:
     return hashlib.sha256(np.ascontiguousarray(array).tobytes()).hexdigest()
 
 
+# tokens (not a multiple of the 128-row tile), model_dim (not a multiple of the
+# 64-wide K slice), heads, eps, seed
+QKV_CASE = (70, 160, 2, 1e-5, 20261202)
+
+
+def make_qkv_fixture(torch) -> None:
+    from tools.reference.dit_block import FixedMMAttention
+
+    tokens, model_dim, heads, eps, seed = QKV_CASE
+    head_dim = 128
+    gen = torch.Generator().manual_seed(seed)
+    block = FixedMMAttention((1, 2, 2), (1, 1, 1), 1, model_dim, model_dim, heads, head_dim, eps)
+    with torch.no_grad():
+        block.proj_qkv.vid.weight.copy_(torch.randn(3 * heads * head_dim, model_dim, generator=gen) * 0.08)
+        block.norm_q.vid.weight.copy_(1.0 + 0.25 * torch.randn(head_dim, generator=gen))
+        block.norm_k.vid.weight.copy_(1.0 + 0.25 * torch.randn(head_dim, generator=gen))
+        block.proj_qkv.vid.to(torch.bfloat16)  # the bf16 blocks: bf16 Linear, fp32 RMSNorm weights
+        x = torch.randn(tokens, model_dim, generator=gen).bfloat16()
+        # FixedMMAttention.forward, dit_block.py:280-287 (video branch)
+        qkv = block.proj_qkv.vid(x).reshape(-1, 3, heads, head_dim)
+        q, k, v = qkv.unbind(dim=1)
+        out = torch.stack((block.norm_q.vid(q), block.norm_k.vid(k), v.float()), dim=1)
+    np.savez_compressed(
+        os.path.join(HERE, "qkv_project.npz"), tokens=tokens, model_dim=model_dim, heads=heads, eps=eps, seed=seed,
+        x=x.float().numpy(), w=block.proj_qkv.vid.weight.detach().float().numpy(),
+        gamma_q=block.norm_q.vid.weight.detach().float().numpy(),
+        gamma_k=block.norm_k.vid.weight.detach().float().numpy(), out=out.float().numpy())
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--only", choices=["qkv"], default=None)
     args = parser.parse_args()
     sys.path.insert(0, args.reference)
     import torch
+
+    make_qkv_fixture(torch)
+    if args.only == "qkv":
+        print("wrote qkv_project.npz to", HERE)
+        return
     from tools.reference.awa_attention import AwaAttentionPack, AwaAttentionUnpack, AwaWindowAttention
     from tools.reference.dit_block import _apply_fixed_rotary, build_mmrope_frequencies
     from tools.reference.seedvr2_baseline import awa_round_trip, make_windows
