@@ -27,6 +27,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import multiprocessing as mp
 import os
 import statistics
@@ -398,6 +399,93 @@ def run_b200(args, rank, world, local_rank):
     return line
 
 
+MODEL_DIM = 2560  # vid_dim of the 3B DiT: proj_qkv is 2560 -> 3 x 20 x 128
+
+
+def run_qkv_proj(args, rank, world, local_rank):
+    """--stage qkv-proj: the producer of the AWA input (awa_qkv_project) on the
+    workload's video rows: x [N_v, 2560] W^T -> [N_v, 7680] with the per-head
+    RMSNorm of Q and K; a step is one projection, inputs resident in HBM."""
+    import torch
+    import torch.distributed as dist
+
+    import awa_b200
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    grid = WORKLOADS[args.workload][0]
+    n_v = grid[0] * grid[1] * grid[2]
+    n_out = 3 * HEADS * HEAD_DIM
+    gen = torch.Generator(device=device).manual_seed(4321 + rank)
+    x = torch.randn(n_v, MODEL_DIM, device=device, generator=gen).bfloat16()
+    w = (torch.randn(n_out, MODEL_DIM, device=device, generator=gen) / math.sqrt(MODEL_DIM)).bfloat16()
+    gq = 1.0 + 0.25 * torch.randn(HEAD_DIM, device=device, generator=gen)
+    gk = 1.0 + 0.25 * torch.randn(HEAD_DIM, device=device, generator=gen)
+    out = torch.empty(n_v, 3, HEADS, HEAD_DIM, device=device, dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        awa_b200.qkv_project(x, w, gq, gk, 1e-5, HEADS, out=out, stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    clocks = ClockSampler(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                          int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank]))
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    awa_b200.device_status()
+    awa_b200.profile_reset()
+    awa_b200.profile_enable(True)
+    barrier()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    stop.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clock = clocks.stop()
+    awa_b200.profile_enable(False)
+    prof = awa_b200.profile_collect()
+    t = torch.tensor([start.elapsed_time(stop)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_step = float(t.item()) / args.steps
+    awa_b200.device_status()
+    flops = 2.0 * n_v * MODEL_DIM * n_out
+    launches, kernel_total = prof.get("awa_qkv_project", (0, 0.0))
+    kernel_ms = kernel_total / max(launches, 1)
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    tensor_peak = peaks.get("bf16_tflops")
+    peak_src = "measured" if tensor_peak else "fallback"
+    tensor_peak = tensor_peak or 1590.0
+    achieved = flops / (kernel_ms / 1000.0) / 1e12
+    return {
+        "metric": "QKV projection + per-head RMSNorm (producer of the AWA input) TFLOP/s per B200",
+        "value": round(flops * world / (ms_per_step / 1000.0) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1) x, W ~ N(0, 1/2560)",
+        "config": {"workload": f"{args.workload}-qkv-proj", "tokens": n_v, "model_dim": MODEL_DIM,
+                   "out_features": n_out, "heads": HEADS, "head_dim": HEAD_DIM,
+                   "l2": f"x {n_v * MODEL_DIM * 2 / 1e9:.2f} GB + out {n_v * n_out * 2 / 1e9:.2f} GB per step > 126 MB L2"},
+        "gpu_launches": sum(v[0] for v in prof.values()),
+        "roofline": {"bound": "tensor", "kernel": "awa_qkv_project", "achieved": round(achieved, 1),
+                     "peak": tensor_peak, "unit": "TFLOP/s", "frac": round(achieved / tensor_peak, 4),
+                     "traffic": None, "peak_source": peak_src, "kernel_ms": round(kernel_ms, 5),
+                     "flops": flops},
+        "clocks": clock,
+    }
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -408,6 +496,8 @@ def main():
     parser.add_argument("--e2e-steps", type=int, default=20)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiler captures)")
+    parser.add_argument("--stage", default="awa", choices=["awa", "qkv-proj"],
+                        help="awa: the AWA layer (the headline); qkv-proj: its input's producer")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
@@ -431,6 +521,11 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if args.stage == "qkv-proj":
+            line = run_qkv_proj(args, rank, world, local_rank)
+            if rank == 0:
+                print(json.dumps(line), flush=True)
+            return
         line = run_b200(args, rank, world, local_rank)
         if rank == 0:
             if world == 1 and not args.no_cpu_baseline:
