@@ -241,6 +241,25 @@ int awa_qkv_project(int tokens, int model_dim, int heads, int head_dim, const vo
                     const void* w, int64_t w_stride, const float* gamma_q, const float* gamma_k, float eps,
                     int out_dtype, void* out, int64_t out_stride, awa_stream_t stream);
 
+/* The consumer of the AWA output, on the tensor cores: for one branch of a DiT
+ * block, proj_out (a Linear with bias, tools/reference/dit_block.py:299), the
+ * Ada "out" gate (FixedAdaBranch.forward mode "out", :187-190) and the
+ * residual add (FixedDitBlock.forward :345-347):
+ *   out[t][c] = residual[t][c] + bf16(x[t] W^T + bias)[c] * gate[c]
+ * with (hidden * gate) and the sum each rounded to fp32, as the reference.
+ *   x:        tokens rows of in_dim bf16 (the AWA output rows, heads*head_dim),
+ *             x_stride elements apart (16-byte rows)
+ *   w:        out_dim rows of in_dim bf16 ([out][in], nn.Linear's layout)
+ *   bias, gate: out_dim fp32 (gate: the block's gate_a + gate_b for this step)
+ *   residual: tokens rows of out_dim, residual_dtype (AWA_BF16 or AWA_F32),
+ *             16-byte aligned rows (the block's input)
+ *   out:      tokens rows of out_dim out_dtype, 32-byte aligned rows.
+ * out_dim must be a multiple of 128. */
+int awa_out_project(int tokens, int in_dim, int out_dim, const void* x, int64_t x_stride, const void* w,
+                    int64_t w_stride, const float* bias, const float* gate, const void* residual,
+                    int64_t residual_stride, int residual_dtype, int out_dtype, void* out, int64_t out_stride,
+                    awa_stream_t stream);
+
 /* Device-side status of the library on the current device: 0, or the code of
  * the first device check that failed since the last call (a bounded wait that
  * gave up). Synchronises the device. Clears the flag. */

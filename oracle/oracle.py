@@ -203,6 +203,19 @@ def qkv_project(x: np.ndarray, w: np.ndarray, gamma_q: np.ndarray, gamma_k: np.n
     return y
 
 
+def out_project(x: np.ndarray, w: np.ndarray, bias: np.ndarray, gate: np.ndarray, residual: np.ndarray) -> np.ndarray:
+    """The consumer of the AWA output: a DiT block's proj_out, Ada "out" gate
+    and residual (tools/reference/dit_block.py:299 -- nn.Linear with bias, bf16
+    output in the bf16 blocks; FixedAdaBranch.forward mode "out" :187-190 --
+    hidden * (gate_a + gate_b); FixedDitBlock.forward :345-347 -- + the block
+    input). x [tokens, in_dim], w [out_dim, in_dim] hold bf16 values as fp32;
+    gate is gate_a + gate_b. Returns [tokens, out_dim] fp32: the product and the
+    sum each rounded to fp32."""
+    linear = round_bf16_rne(np.asarray(x, np.float32) @ np.asarray(w, np.float32).T + np.asarray(bias, np.float32))
+    gated = (linear * np.asarray(gate, np.float32)).astype(np.float32)
+    return (gated + np.asarray(residual, np.float32)).astype(np.float32)
+
+
 class Reference:
     """The reference's own awa_layers.cpp CPU forward (oracle/_ref)."""
 

@@ -38,7 +38,7 @@ EXPORTED_SYMBOLS = (
     "awa_pack", "awa_mmrope", "awa_window_attention", "awa_unpack", "awa_forward_workspace_bytes", "awa_forward",
     "awa_forward_noalloc",
     "awa_forward_windows", "awa_text_finalize", "awa_scatter_video_shard", "awa_gather_video_shard",
-    "awa_window_range_video_rows", "awa_partition_windows", "awa_qkv_project", "awa_device_status",
+    "awa_window_range_video_rows", "awa_partition_windows", "awa_qkv_project", "awa_out_project", "awa_device_status",
     "awa_attention_kernel_kind",
     "awa_profile_enable", "awa_profile_reset", "awa_profile_collect", "awa_last_error", "awa_version",
 )
@@ -96,6 +96,7 @@ def library() -> ctypes.CDLL:
         "awa_forward": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p, sz, p]),
         "awa_forward_noalloc": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p]),
         "awa_qkv_project": (i, [i, i, i, i, p, i64, p, i64, p, p, ctypes.c_float, i, p, i64, p]),
+        "awa_out_project": (i, [i, i, i, p, i64, p, i64, p, p, p, i64, i, i, p, i64, p]),
         "awa_forward_windows": (i, [p, i, i, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, p, sz, p]),
         "awa_text_finalize": (i, [p, i, i, p, i, p, i64, p]),
         "awa_scatter_video_shard": (i, [p, i, i, i, i, i, p, p, i64, p]),
@@ -377,6 +378,23 @@ def qkv_project(x, w, gamma_q, gamma_k, eps: float, heads: int, out_dtype=None, 
     return out
 
 
+def out_project(x, w, bias, gate, residual, out_dtype=None, out=None, stream=None):
+    """The block's proj_out + Ada "out" gate + residual (awa_out_project):
+    x [tokens, in_dim] bf16, w [out_dim, in_dim] bf16, bias / gate [out_dim]
+    fp32, residual [tokens, out_dim] bf16 or fp32 -> residual + bf16(x W^T +
+    bias) * gate, [tokens, out_dim] in out_dtype (the residual's by default)."""
+    torch = _torch()
+    tokens, in_dim = x.shape
+    out_dim = w.shape[0]
+    if out is None:
+        out = torch.empty(tokens, out_dim, dtype=out_dtype or residual.dtype, device=x.device)
+    _check(library().awa_out_project(tokens, in_dim, out_dim, x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0),
+                                     bias.data_ptr(), gate.data_ptr(), residual.data_ptr(), residual.stride(0),
+                                     _dtype_code(residual), _dtype_code(out), out.data_ptr(), out.stride(0),
+                                     _stream_ptr(stream)))
+    return out
+
+
 def device_status() -> None:
     """Raise if a device-side check of the library failed since the last call."""
     _check(library().awa_device_status())
@@ -459,4 +477,4 @@ def ncnn_run_chain(params: Sequence[int], heads: int, head_dim: int, video_qkv, 
 
 
 __all__ = ["AwaPlan", "AwaError", "PlanInfo", "library", "make_windows", "device_status", "ncnn_run_chain",
-           "EXPORTED_SYMBOLS", "qkv_project", "AWA_F32", "AWA_BF16", "AWA_PREC_FP32", "AWA_PREC_BF16"]
+           "EXPORTED_SYMBOLS", "qkv_project", "out_project", "AWA_F32", "AWA_BF16", "AWA_PREC_FP32", "AWA_PREC_BF16"]

@@ -127,6 +127,11 @@ int launch_attention_tc(const AttnArgs& args, int packed, int in_dtype, int out_
 int launch_qkv_project(int tokens, int model_dim, int heads, const void* x, int64_t x_stride, const void* w,
                        int64_t w_stride, const float* gamma_q, const float* gamma_k, float eps, int out_dtype,
                        void* out, int64_t out_stride, cudaStream_t stream);
+// out = resid + bf16(x W^T + bias) * gate per output channel (n_out % 128 == 0);
+// arguments checked by the caller.
+int launch_out_project(int tokens, int k_dim, int n_out, const void* x, int64_t x_stride, const void* w,
+                       int64_t w_stride, const float* bias, const float* gate, const void* resid, int64_t resid_stride,
+                       int resid_dtype, int out_dtype, void* out, int64_t out_stride, cudaStream_t stream);
 
 int* device_error_flag();  // per-device flag in device memory
 // Sets the calling thread's awa_last_error() text; returns code.

@@ -866,6 +866,27 @@ int awa_qkv_project(int tokens, int model_dim, int heads, int head_dim, const vo
                          "awa_qkv_project launch");
 }
 
+int awa_out_project(int tokens, int in_dim, int out_dim, const void* x, int64_t x_stride, const void* w,
+                    int64_t w_stride, const float* bias, const float* gate, const void* residual,
+                    int64_t residual_stride, int residual_dtype, int out_dtype, void* out, int64_t out_stride,
+                    awa_stream_t stream)
+{
+    if (tokens <= 0 || in_dim <= 0 || out_dim <= 0 || out_dim % 128 || !x || !w || !bias || !gate || !residual ||
+        !out || !valid_dtype(out_dtype) || !valid_dtype(residual_dtype) || x_stride < in_dim ||
+        w_stride < in_dim || out_stride < out_dim || residual_stride < out_dim)
+        return fail(AWA_ERR_INVALID, "awa_out_project: invalid sizes (out_dim a multiple of 128), dtype or NULL");
+    const size_t osz = dtype_size(out_dtype), rsz = dtype_size(residual_dtype);
+    if (!is_aligned16(x) || !is_aligned16(w) || !is_aligned16(residual) || (x_stride * 2) % 16 ||
+        (w_stride * 2) % 16 || (residual_stride * (int64_t)rsz) % 16 || reinterpret_cast<uintptr_t>(out) % 32 ||
+        (out_stride * (int64_t)osz) % 32)
+        return fail(AWA_ERR_INVALID,
+                    "awa_out_project: x, w, residual need 16-byte aligned rows, out 32-byte aligned rows");
+    return launch_status(awa::launch_out_project(tokens, in_dim, out_dim, x, x_stride, w, w_stride, bias, gate,
+                                                 residual, residual_stride, residual_dtype, out_dtype, out,
+                                                 out_stride, static_cast<cudaStream_t>(stream)),
+                         "awa_out_project launch");
+}
+
 int64_t awa_window_range_video_rows(const awa_plan* plan, int window_begin, int window_end)
 {
     if (!plan || window_begin < 0 || window_end > plan->info.window_count || window_begin > window_end)

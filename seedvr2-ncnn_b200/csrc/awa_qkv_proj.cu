@@ -1,6 +1,11 @@
-// awa_qkv_proj.cu -- the producer of the AWA layer's input on the tensor cores:
-// the QKV projection of a DiT block, x W^T (bf16 operands, fp32 accumulation
-// in TMEM), with the per-head RMSNorm of Q and K in the epilogue.
+// awa_qkv_proj.cu -- the two GEMMs either side of the AWA layer on the tensor
+// cores, x W^T with bf16 operands and fp32 accumulation in TMEM, each with its
+// block's elementwise work in the epilogue:
+//   kQkv  the producer of the AWA input: the QKV projection with the per-head
+//         RMSNorm of Q and K (below);
+//   kOut  the consumer of the AWA output: proj_out (Linear with bias), the Ada
+//         "out" gate and the residual add (dit_block.py:299, 187-190, 345-347):
+//         out = residual + bf16(x W^T + bias) * gate, per output channel.
 //
 // Math of the reference block (tools/reference/dit_block.py:280-287): the
 // Linear proj_qkv (bias-free, bf16 output), then nn.RMSNorm(head_dim, eps,
@@ -50,13 +55,24 @@ constexpr uint32_t kTmemColumns = 2 * kTileN;  // two accumulators
 constexpr uint64_t kWaitLimitNs = 4000000000ull;
 constexpr uint64_t kDrainLimitNs = 200000000ull;
 
+enum EpiMode : int
+{
+    kQkv = 0,
+    kOut = 1
+};
+
 struct ProjArgs
 {
-    int tokens, model_dim, heads, n_out;  // n_out = 3 * heads * 128
+    int tokens, model_dim, heads, n_out;  // kQkv: n_out = 3 * heads * 128
     int tiles_n, tiles, k_steps;
-    const float* gamma_q;
+    const float* gamma_q;  // kQkv
     const float* gamma_k;
     float eps;
+    const float* bias;  // kOut: n_out channels each
+    const float* gate;
+    const void* resid;  // kOut: tokens rows of n_out
+    int64_t resid_stride;
+    int resid_f32;
     void* out;
     int64_t out_stride;  // elements
     int out_f32;
@@ -231,7 +247,135 @@ __device__ void mma_role(const ProjArgs& p, ProjShared& sh, uint32_t tmem)
     drain_bar(&sh.mma_done, 0, p.error_flag, 65);
 }
 
+// 16 consecutive residual values of a row (bf16 or fp32) into fp32.
+__device__ __forceinline__ void load_resid16(const ProjArgs& p, int64_t offset, float* dst)
+{
+    if (p.resid_f32)
+    {
+        const uint4* q = reinterpret_cast<const uint4*>(static_cast<const float*>(p.resid) + offset);
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+        {
+            const uint4 w = __ldg(q + u);
+            dst[4 * u] = __uint_as_float(w.x);
+            dst[4 * u + 1] = __uint_as_float(w.y);
+            dst[4 * u + 2] = __uint_as_float(w.z);
+            dst[4 * u + 3] = __uint_as_float(w.w);
+        }
+    }
+    else
+    {
+        const uint4* q = reinterpret_cast<const uint4*>(static_cast<const bf16*>(p.resid) + offset);
+#pragma unroll
+        for (int u = 0; u < 2; u++)
+        {
+            const uint4 w = __ldg(q + u);
+            const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+            {
+                dst[8 * u + 2 * k] = __uint_as_float(words[k] << 16);
+                dst[8 * u + 2 * k + 1] = __uint_as_float(words[k] & 0xffff0000u);
+            }
+        }
+    }
+}
+
+// 32 values of a row into out_dtype at dst (32-byte aligned).
+__device__ __forceinline__ void store32(const ProjArgs& p, char* dst, const float* v)
+{
+    if (p.out_f32)
+    {
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+        {
+            uint32_t w[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                w[u] = __float_as_uint(v[8 * k + u]);
+            st_v8(dst + 32 * k, w);
+        }
+    }
+    else
+    {
+#pragma unroll
+        for (int k = 0; k < 2; k++)
+        {
+            uint32_t w[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+            {
+                const __nv_bfloat162 pr = __floats2bfloat162_rn(v[16 * k + 2 * u], v[16 * k + 2 * u + 1]);
+                w[u] = *reinterpret_cast<const uint32_t*>(&pr);
+            }
+            st_v8(dst + 32 * k, w);
+        }
+    }
+}
+
+// kOut: out = residual + bf16(acc + bias) * gate, 32 columns at a time.
+__device__ void epilogue_out(const ProjArgs& p, ProjShared& sh, uint32_t tmem)
+{
+    const int warp = threadIdx.x >> 5;
+    const int row = (warp & 3) * 32 + (threadIdx.x & 31);  // = TMEM lane
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    volatile int* abort = &sh.abort;
+    const int osz = p.out_f32 ? 4 : 2;
+    int i = 0;
+    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, i++)
+    {
+        const int buf = i & 1;
+        if (!warp_all(wait_bar(&sh.acc_full[buf], (i >> 1) & 1, abort, p.error_flag, 67)))
+            return;
+        tc::fence_after_sync();
+        const int token = (t / p.tiles_n) * kTileM + row;
+        const int n0 = (t % p.tiles_n) * kTileN;
+#pragma unroll 1
+        for (int c = 0; c < kTileN / 32; c++)
+        {
+            const int f0 = n0 + 32 * c;
+            uint32_t r[32];
+            tc::tmem_ld32(tmem + lane_base + (uint32_t)(buf * kTileN + 32 * c), r);
+            tc::tmem_wait_ld();
+            if (token >= p.tokens || f0 >= p.n_out)
+                continue;
+            float v[32];
+#pragma unroll
+            for (int half = 0; half < 2; half++)
+            {
+                float res[16];
+                load_resid16(p, (int64_t)token * p.resid_stride + f0 + 16 * half, res);
+#pragma unroll
+                for (int u = 0; u < 16; u++)
+                {
+                    const int k = 16 * half + u;
+                    // bf16 Linear output (bias added first), then the two fp32
+                    // roundings of hidden * gate + residual
+                    v[k] = __fadd_rn(__fmul_rn(round_bf16(__uint_as_float(r[k]) + __ldg(p.bias + f0 + k)),
+                                               __ldg(p.gate + f0 + k)),
+                                     res[u]);
+                }
+            }
+            store32(p, static_cast<char*>(p.out) + ((int64_t)token * p.out_stride + f0) * osz, v);
+        }
+        tc::fence_before_sync();
+        arrive(&sh.acc_empty[buf]);
+    }
+}
+
+__device__ void epilogue_qkv(const ProjArgs& p, ProjShared& sh, uint32_t tmem);
+
+template <int MODE>
 __device__ void epilogue_role(const ProjArgs& p, ProjShared& sh, uint32_t tmem)
+{
+    if (MODE == kOut)
+        epilogue_out(p, sh, tmem);
+    else
+        epilogue_qkv(p, sh, tmem);
+}
+
+// kQkv: one head (128 columns) at a time: bf16 Linear output, RMSNorm of Q/K.
+__device__ void epilogue_qkv(const ProjArgs& p, ProjShared& sh, uint32_t tmem)
 {
     const int warp = threadIdx.x >> 5;
     const int row = (warp & 3) * 32 + (threadIdx.x & 31);  // = TMEM lane
@@ -260,10 +404,13 @@ __device__ void epilogue_role(const ProjArgs& p, ProjShared& sh, uint32_t tmem)
                 tc::tmem_wait_ld();
 #pragma unroll
                 for (int k = 0; k < 32; k++)
-                    v[32 * c + k] = round_bf16(__uint_as_float(r[k]));  // the Linear's bf16 output
+                    v[32 * c + k] = __uint_as_float(r[k]);
             }
             if (token >= p.tokens || f0 >= p.n_out)
                 continue;
+#pragma unroll
+            for (int k = 0; k < 128; k++)
+                v[k] = round_bf16(v[k]);  // the Linear's bf16 output
             if (f0 < qk_cols)
             {
                 // RMSNorm over the head: fp32 squares and sum (four partial sums)
@@ -311,6 +458,7 @@ __device__ void epilogue_role(const ProjArgs& p, ProjShared& sh, uint32_t tmem)
     }
 }
 
+template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) qkv_proj_kernel(const ProjArgs p, const __grid_constant__ ProjMaps maps)
 {
     extern __shared__ uint8_t smem_raw[];
@@ -352,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1) qkv_proj_kernel(const ProjArgs p,
     else if (warp == kMmaWarp)
         mma_role(p, sh, tmem);
     else
-        epilogue_role(p, sh, tmem);
+        epilogue_role<MODE>(p, sh, tmem);
     tc::fence_before_sync();
     __syncthreads();
     if (warp == kMmaWarp)
@@ -433,17 +581,60 @@ int launch_qkv_project(int tokens, int model_dim, int heads, const void* x, int6
     p.gamma_q = gamma_q;
     p.gamma_k = gamma_k;
     p.eps = eps;
+    p.bias = p.gate = nullptr;
+    p.resid = nullptr;
+    p.resid_stride = 0;
+    p.resid_f32 = 0;
     p.out = out;
     p.out_stride = out_stride;
     p.out_f32 = out_dtype == kF32;
     p.error_flag = device_error_flag();
     const size_t smem = sizeof(ProjShared) + 1024;
-    cudaError_t err = cudaFuncSetAttribute(qkv_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t err =
+        cudaFuncSetAttribute(qkv_proj_kernel<kQkv>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess)
         return (int)err;
     ProfileScope prof("awa_qkv_project", stream);
     const int grid = p.tiles < sm_count_proj() ? p.tiles : sm_count_proj();
-    qkv_proj_kernel<<<grid, kThreads, smem, stream>>>(p, maps);
+    qkv_proj_kernel<kQkv><<<grid, kThreads, smem, stream>>>(p, maps);
+    return (int)cudaGetLastError();
+}
+
+int launch_out_project(int tokens, int k_dim, int n_out, const void* x, int64_t x_stride, const void* w,
+                       int64_t w_stride, const float* bias, const float* gate, const void* resid, int64_t resid_stride,
+                       int resid_dtype, int out_dtype, void* out, int64_t out_stride, cudaStream_t stream)
+{
+    ProjMaps maps;
+    if (!encode_matrix(&maps.x, x, tokens, k_dim, x_stride, kTileM) ||
+        !encode_matrix(&maps.w, w, n_out, k_dim, w_stride, kTileN))
+        return (int)cudaErrorInvalidValue;
+    ProjArgs p;
+    p.tokens = tokens;
+    p.model_dim = k_dim;
+    p.heads = 0;
+    p.n_out = n_out;
+    p.tiles_n = (n_out + kTileN - 1) / kTileN;
+    p.tiles = ((tokens + kTileM - 1) / kTileM) * p.tiles_n;
+    p.k_steps = (k_dim + kTileK - 1) / kTileK;
+    p.gamma_q = p.gamma_k = nullptr;
+    p.eps = 0.f;
+    p.bias = bias;
+    p.gate = gate;
+    p.resid = resid;
+    p.resid_stride = resid_stride;
+    p.resid_f32 = resid_dtype == kF32;
+    p.out = out;
+    p.out_stride = out_stride;
+    p.out_f32 = out_dtype == kF32;
+    p.error_flag = device_error_flag();
+    const size_t smem = sizeof(ProjShared) + 1024;
+    cudaError_t err =
+        cudaFuncSetAttribute(qkv_proj_kernel<kOut>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess)
+        return (int)err;
+    ProfileScope prof("awa_out_project", stream);
+    const int grid = p.tiles < sm_count_proj() ? p.tiles : sm_count_proj();
+    qkv_proj_kernel<kOut><<<grid, kThreads, smem, stream>>>(p, maps);
     return (int)cudaGetLastError();
 }
 

@@ -19,7 +19,11 @@ HGinkgo/SeedVR2-ncnn and records, for each configuration:
   FixedMMAttention (dit_block.py:234-263) as its forward does (:280-287): the
   bf16 proj_qkv Linear, then norm_q / norm_k (FixedRMSNorm) on Q and K.
 
-``--only qkv`` writes just the last one.
+* ``out_project.npz``: the consumer of the AWA output, run with the modules of
+  FixedDitBlock (dit_block.py:302-349): attn.proj_out (a Linear with bias), the
+  Ada "out" gate of ada.vid (:178-190) and the residual add (:345-347).
+
+``--only gemms`` writes just these two.
 
 The fixtures are small (a few hundred KB) and are what the CPU tests compare the
 C oracle against; the GPU tests never read the reference.
@@ -100,17 +104,50 @@ def make_qkv_fixture(torch) -> None:
         gamma_k=block.norm_k.vid.weight.detach().float().numpy(), out=out.float().numpy())
 
 
+# tokens (not a multiple of 128), in_dim (heads * 128), out_dim (= vid_dim), seed
+OUT_CASE = (70, 256, 256, 20261203)
+
+
+def make_out_fixture(torch) -> None:
+    from tools.reference.dit_block import FixedDitBlock
+
+    tokens, in_dim, dim, seed = OUT_CASE
+    gen = torch.Generator().manual_seed(seed)
+    block = FixedDitBlock(source_shape=(1, 2, 2), window_shape=(1, 1, 1), text_tokens=1, vid_dim=dim, txt_dim=dim,
+                          emb_dim=6 * dim, heads=in_dim // 128, head_dim=128)
+    with torch.no_grad():
+        proj = block.attn.proj_out.vid
+        proj.weight.copy_(torch.randn(dim, in_dim, generator=gen) * 0.06)
+        proj.bias.copy_(torch.randn(dim, generator=gen) * 0.1)
+        block.ada.vid.attn_gate.copy_(torch.randn(dim, generator=gen) * 0.2)
+        proj.to(torch.bfloat16)  # the bf16 blocks
+        emb = torch.randn(1, 6 * dim, generator=gen)
+        attn_out = torch.randn(tokens, in_dim, generator=gen).bfloat16()
+        vid = torch.randn(tokens, dim, generator=gen)  # the block input (residual), fp32
+        # FixedDitBlock.forward :340-347 after the attention: proj_out, Ada "out", residual
+        hidden = proj(attn_out)
+        gated = block.ada.vid(hidden, emb, "attn", "out")
+        out = gated + vid
+        modulation = emb.reshape(1, dim, 2, 3)[0, :, 0, :]
+        gate = modulation[:, 2] + block.ada.vid.attn_gate
+    np.savez_compressed(
+        os.path.join(HERE, "out_project.npz"), tokens=tokens, in_dim=in_dim, dim=dim, seed=seed,
+        x=attn_out.float().numpy(), w=proj.weight.detach().float().numpy(), bias=proj.bias.detach().float().numpy(),
+        gate=gate.detach().float().numpy(), residual=vid.numpy(), out=out.float().numpy())
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", default="/root/reference")
-    parser.add_argument("--only", choices=["qkv"], default=None)
+    parser.add_argument("--only", choices=["gemms"], default=None)
     args = parser.parse_args()
     sys.path.insert(0, args.reference)
     import torch
 
     make_qkv_fixture(torch)
-    if args.only == "qkv":
-        print("wrote qkv_project.npz to", HERE)
+    make_out_fixture(torch)
+    if args.only == "gemms":
+        print("wrote qkv_project.npz and out_project.npz to", HERE)
         return
     from tools.reference.awa_attention import AwaAttentionPack, AwaAttentionUnpack, AwaWindowAttention
     from tools.reference.dit_block import _apply_fixed_rotary, build_mmrope_frequencies

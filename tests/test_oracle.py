@@ -155,3 +155,14 @@ def test_qkv_project_oracle_matches_reference_fixture():
     # (near-cancelling dot products move by more than one ulp of their value)
     assert int((rounded != ref).sum()) <= ref.size // 1000
     assert float(np.linalg.norm(rounded - ref) / np.linalg.norm(ref)) < 1e-5
+
+
+def test_out_project_oracle_matches_reference_fixture():
+    """The consumer's restatement against FixedDitBlock's own proj_out, Ada
+    "out" gate and residual run (tests/golden/out_project.npz, tokens 70,
+    256 -> 256): bit-exact."""
+    from oracle.oracle import out_project
+
+    f = np.load(os.path.join(os.path.dirname(__file__), "golden", "out_project.npz"))
+    out = out_project(f["x"], f["w"], f["bias"], f["gate"], f["residual"])
+    assert np.array_equal(out, f["out"])
