@@ -405,7 +405,10 @@ MODEL_DIM = 2560  # vid_dim of the 3B DiT: proj_qkv is 2560 -> 3 x 20 x 128
 def run_qkv_proj(args, rank, world, local_rank):
     """--stage qkv-proj: the producer of the AWA input (awa_qkv_project) on the
     workload's video rows: x [N_v, 2560] W^T -> [N_v, 7680] with the per-head
-    RMSNorm of Q and K; a step is one projection, inputs resident in HBM."""
+    RMSNorm of Q and K. --stage out-proj: the consumer of the AWA output
+    (awa_out_project): the AWA output [N_v, 2560] W_out^T + bias, times the Ada
+    gate, plus the residual [N_v, 2560]. A step is one GEMM, inputs resident in
+    HBM."""
     import torch
     import torch.distributed as dist
 
@@ -415,17 +418,27 @@ def run_qkv_proj(args, rank, world, local_rank):
     torch.cuda.set_device(device)
     grid = WORKLOADS[args.workload][0]
     n_v = grid[0] * grid[1] * grid[2]
-    n_out = 3 * HEADS * HEAD_DIM
+    producer = args.stage == "qkv-proj"
+    n_out = 3 * HEADS * HEAD_DIM if producer else MODEL_DIM
     gen = torch.Generator(device=device).manual_seed(4321 + rank)
     x = torch.randn(n_v, MODEL_DIM, device=device, generator=gen).bfloat16()
     w = (torch.randn(n_out, MODEL_DIM, device=device, generator=gen) / math.sqrt(MODEL_DIM)).bfloat16()
-    gq = 1.0 + 0.25 * torch.randn(HEAD_DIM, device=device, generator=gen)
-    gk = 1.0 + 0.25 * torch.randn(HEAD_DIM, device=device, generator=gen)
-    out = torch.empty(n_v, 3, HEADS, HEAD_DIM, device=device, dtype=torch.bfloat16)
     stream = torch.cuda.current_stream(device)
+    if producer:
+        gq = 1.0 + 0.25 * torch.randn(HEAD_DIM, device=device, generator=gen)
+        gk = 1.0 + 0.25 * torch.randn(HEAD_DIM, device=device, generator=gen)
+        out = torch.empty(n_v, 3, HEADS, HEAD_DIM, device=device, dtype=torch.bfloat16)
 
-    def step():
-        awa_b200.qkv_project(x, w, gq, gk, 1e-5, HEADS, out=out, stream=stream)
+        def step():
+            awa_b200.qkv_project(x, w, gq, gk, 1e-5, HEADS, out=out, stream=stream)
+    else:
+        bias = 0.1 * torch.randn(n_out, device=device, generator=gen)
+        gate = 0.2 * torch.randn(n_out, device=device, generator=gen)
+        resid = torch.randn(n_v, n_out, device=device, generator=gen).bfloat16()
+        out = torch.empty(n_v, n_out, device=device, dtype=torch.bfloat16)
+
+        def step():
+            awa_b200.out_project(x, w, bias, gate, resid, out=out, stream=stream)
 
     def barrier():
         if world > 1:
@@ -457,7 +470,8 @@ def run_qkv_proj(args, rank, world, local_rank):
     ms_per_step = float(t.item()) / args.steps
     awa_b200.device_status()
     flops = 2.0 * n_v * MODEL_DIM * n_out
-    launches, kernel_total = prof.get("awa_qkv_project", (0, 0.0))
+    kernel_name = "awa_qkv_project" if producer else "awa_out_project"
+    launches, kernel_total = prof.get(kernel_name, (0, 0.0))
     kernel_ms = kernel_total / max(launches, 1)
     peaks = {}
     try:
@@ -483,19 +497,20 @@ def run_qkv_proj(args, rank, world, local_rank):
     torch.cuda.synchronize()
     gemm_ms = g0.elapsed_time(g1) / args.steps
     return {
-        "metric": "QKV projection + per-head RMSNorm (producer of the AWA input) TFLOP/s per B200",
+        "metric": ("QKV projection + per-head RMSNorm (producer of the AWA input)" if producer else
+                   "proj_out + Ada gate + residual (consumer of the AWA output)") + " TFLOP/s per B200",
         "value": round(flops * world / (ms_per_step / 1000.0) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1) x, W ~ N(0, 1/2560)",
-        "config": {"workload": f"{args.workload}-qkv-proj", "tokens": n_v, "model_dim": MODEL_DIM,
+        "config": {"workload": f"{args.workload}-{args.stage}", "tokens": n_v, "in_features": MODEL_DIM,
                    "out_features": n_out, "heads": HEADS, "head_dim": HEAD_DIM,
                    "l2": f"x {n_v * MODEL_DIM * 2 / 1e9:.2f} GB + out {n_v * n_out * 2 / 1e9:.2f} GB per step > 126 MB L2"},
         "gpu_launches": sum(v[0] for v in prof.values()),
-        "roofline": {"bound": "tensor", "kernel": "awa_qkv_project", "achieved": round(achieved, 1),
+        "roofline": {"bound": "tensor", "kernel": kernel_name, "achieved": round(achieved, 1),
                      "peak": tensor_peak, "unit": "TFLOP/s", "frac": round(achieved / tensor_peak, 4),
                      "traffic": None, "peak_source": peak_src, "kernel_ms": round(kernel_ms, 5),
                      "flops": flops},
-        "library_gemm": {"what": "cuBLAS GEMM alone via torch.mm (no RMSNorm), same operands", "ms": round(gemm_ms, 5),
+        "library_gemm": {"what": "cuBLAS GEMM alone via torch.mm (no epilogue), same operands", "ms": round(gemm_ms, 5),
                          "tflops": round(flops / (gemm_ms / 1000.0) / 1e12, 1)},
         "clocks": clock,
     }
@@ -511,8 +526,9 @@ def main():
     parser.add_argument("--e2e-steps", type=int, default=20)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiler captures)")
-    parser.add_argument("--stage", default="awa", choices=["awa", "qkv-proj"],
-                        help="awa: the AWA layer (the headline); qkv-proj: its input's producer")
+    parser.add_argument("--stage", default="awa", choices=["awa", "qkv-proj", "out-proj"],
+                        help="awa: the AWA layer (the headline); qkv-proj / out-proj: its input's producer / "
+                             "its output's consumer")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
@@ -536,7 +552,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.stage == "qkv-proj":
+        if args.stage in ("qkv-proj", "out-proj"):
             line = run_qkv_proj(args, rank, world, local_rank)
             if rank == 0:
                 print(json.dumps(line), flush=True)
