@@ -360,13 +360,7 @@ def run_b200(args, rank, world, local_rank):
     alg_bytes = in_bytes + out_bytes  # read the source QKV once, write the outputs once
     achieved_gbs = alg_bytes / (attn_ms / 1000.0) / 1e9
     achieved_tflops = flops / (attn_ms / 1000.0) / 1e12
-    traffic = None
-    traffic_file = os.path.join(ROOT, "profiles", "traffic.json")
-    try:
-        with open(traffic_file) as f:
-            traffic = json.load(f).get(f"{name}:{attn_name}")
-    except (OSError, ValueError):
-        traffic = None
+    traffic = recorded_traffic(f"{name}:{attn_name}")
     roofline = {
         "bound": "hbm", "kernel": attn_name, "achieved": round(achieved_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
         "frac": round(achieved_gbs / hbm_peak, 4), "traffic": traffic, "peak_source": peak_src,
@@ -400,6 +394,16 @@ def run_b200(args, rank, world, local_rank):
 
 
 MODEL_DIM = 2560  # vid_dim of the 3B DiT: proj_qkv is 2560 -> 3 x 20 x 128
+
+
+def recorded_traffic(key):
+    """DRAM bytes (read + write) of one launch, from the ncu capture recorded
+    in profiles/traffic.json under "<workload>:<kernel>", or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(key)
+    except (OSError, ValueError):
+        return None
 
 
 def run_qkv_proj(args, rank, world, local_rank):
@@ -508,7 +512,8 @@ def run_qkv_proj(args, rank, world, local_rank):
         "gpu_launches": sum(v[0] for v in prof.values()),
         "roofline": {"bound": "tensor", "kernel": kernel_name, "achieved": round(achieved, 1),
                      "peak": tensor_peak, "unit": "TFLOP/s", "frac": round(achieved / tensor_peak, 4),
-                     "traffic": None, "peak_source": peak_src, "kernel_ms": round(kernel_ms, 5),
+                     "traffic": recorded_traffic(f"{args.workload}-{args.stage}:{kernel_name}"),
+                     "peak_source": peak_src, "kernel_ms": round(kernel_ms, 5),
                      "flops": flops},
         "library_gemm": {"what": "cuBLAS GEMM alone via torch.mm (no epilogue), same operands", "ms": round(gemm_ms, 5),
                          "tflops": round(flops / (gemm_ms / 1000.0) / 1e12, 1)},
