@@ -32,7 +32,7 @@ AWA_ERR_DEVICE = -3
 AWA_ERR_ALLOC = -100
 AWA_NOALLOC_SCRATCH_BYTES = 32 << 20  # scratch of awa_forward_noalloc, per GPU
 
-# Every symbol declared in include/awa_b200.h.
+# Every symbol declared in include/awa_b200.h and include/awa_package.h.
 EXPORTED_SYMBOLS = (
     "awa_make_windows", "awa_plan_create", "awa_plan_create_host", "awa_plan_destroy", "awa_plan_get_info", "awa_plan_get_maps",
     "awa_pack", "awa_mmrope", "awa_window_attention", "awa_unpack", "awa_forward_workspace_bytes", "awa_forward",
@@ -41,6 +41,8 @@ EXPORTED_SYMBOLS = (
     "awa_window_range_video_rows", "awa_partition_windows", "awa_qkv_project", "awa_out_project", "awa_device_status",
     "awa_attention_kernel_kind",
     "awa_profile_enable", "awa_profile_reset", "awa_profile_collect", "awa_last_error", "awa_version",
+    "awa_graph_find_chains", "awa_graph_find_chains_file", "awa_graph_make_dynamic", "awa_manifest_validate",
+    "awa_sha256", "awa_sha256_file",
 )
 
 
@@ -61,6 +63,11 @@ class _RuntimeSpec(ctypes.Structure):
 
 class _Window(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in ("t0", "t1", "h0", "h1", "w0", "w1")]
+
+
+class _GraphChain(ctypes.Structure):
+    _fields_ = [("params", _LayerParams)] + [(n, ctypes.c_int) for n in (
+        "dynamic", "pack_line", "rope_line", "attention_line", "unpack_line", "reshape_line", "reshape_height")]
 
 
 class _PlanInfo(ctypes.Structure):
@@ -110,6 +117,12 @@ def library() -> ctypes.CDLL:
         "awa_profile_collect": (i, [p, sz]),
         "awa_last_error": (ctypes.c_char_p, []),
         "awa_version": (ctypes.c_char_p, []),
+        "awa_graph_find_chains": (i, [ctypes.c_char_p, sz, p, i]),
+        "awa_graph_find_chains_file": (i, [ctypes.c_char_p, p, i]),
+        "awa_graph_make_dynamic": (i, [ctypes.c_char_p, sz, p, sz, ctypes.POINTER(sz)]),
+        "awa_manifest_validate": (i, [ctypes.c_char_p, i]),
+        "awa_sha256": (i, [ctypes.c_char_p, sz, p]),
+        "awa_sha256_file": (i, [ctypes.c_char_p, p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -476,5 +489,67 @@ def ncnn_run_chain(params: Sequence[int], heads: int, head_dim: int, video_qkv, 
     return out
 
 
+def _chains(count_fn) -> List[dict]:
+    n = count_fn(None, 0)
+    if n < 0:
+        _check(n)
+    arr = (_GraphChain * max(n, 1))()
+    _check(min(0, count_fn(ctypes.cast(arr, ctypes.c_void_p), n)))
+    out = []
+    for c in arr[:n]:
+        params = {f: getattr(c.params, f) for f, _ in _LayerParams._fields_}
+        out.append({"params": params, **{f: getattr(c, f) for f, _ in _GraphChain._fields_[1:]}})
+    return out
+
+
+def graph_find_chains(text) -> List[dict]:
+    """AWA chains of an ncnn .param text (str or bytes): per chain its ParamDict
+    values ("params", the awa_layer_params fields), "dynamic" and the 1-based
+    line numbers of its layers (awa_graph_find_chains). Host only."""
+    data = text.encode() if isinstance(text, str) else bytes(text)
+    return _chains(lambda buf, cap: library().awa_graph_find_chains(data, len(data), buf, cap))
+
+
+def graph_find_chains_file(path) -> List[dict]:
+    """graph_find_chains on a .param file."""
+    raw = os.fsencode(path)
+    return _chains(lambda buf, cap: library().awa_graph_find_chains_file(raw, buf, cap))
+
+
+def graph_make_dynamic(text) -> str:
+    """The resolution-independent form of a block graph's .param text: the
+    exporter's normalize_dynamic_awa_template (awa_graph_make_dynamic)."""
+    data = text.encode() if isinstance(text, str) else bytes(text)
+    lib = library()
+    needed = ctypes.c_size_t(0)
+    rc = lib.awa_graph_make_dynamic(data, len(data), None, 0, ctypes.byref(needed))
+    if rc not in (AWA_OK, AWA_ERR_ALLOC):
+        _check(rc)
+    out = ctypes.create_string_buffer(needed.value + 1)
+    _check(lib.awa_graph_make_dynamic(data, len(data), ctypes.cast(out, ctypes.c_void_p), len(out),
+                                      ctypes.byref(needed)))
+    return out.raw[:needed.value].decode()
+
+
+def manifest_validate(package_dir, expected_records: int = 0) -> None:
+    """Raise AwaError unless package_dir matches its manifest.sha256
+    (awa_manifest_validate; expected_records 0 = the reference's 75/146 rule)."""
+    _check(library().awa_manifest_validate(os.fsencode(package_dir), int(expected_records)))
+
+
+def sha256(data: bytes) -> str:
+    buf = ctypes.create_string_buffer(65)
+    data = bytes(data)
+    _check(library().awa_sha256(data, len(data), ctypes.cast(buf, ctypes.c_void_p)))
+    return buf.value.decode()
+
+
+def sha256_file(path) -> str:
+    buf = ctypes.create_string_buffer(65)
+    _check(library().awa_sha256_file(os.fsencode(path), ctypes.cast(buf, ctypes.c_void_p)))
+    return buf.value.decode()
+
+
 __all__ = ["AwaPlan", "AwaError", "PlanInfo", "library", "make_windows", "device_status", "ncnn_run_chain",
-           "EXPORTED_SYMBOLS", "qkv_project", "out_project", "AWA_F32", "AWA_BF16", "AWA_PREC_FP32", "AWA_PREC_BF16"]
+           "EXPORTED_SYMBOLS", "qkv_project", "out_project", "graph_find_chains", "graph_find_chains_file",
+           "graph_make_dynamic", "manifest_validate", "sha256", "sha256_file", "AWA_F32", "AWA_BF16", "AWA_PREC_FP32", "AWA_PREC_BF16"]

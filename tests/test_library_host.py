@@ -1,6 +1,6 @@
 """Host-side checks of the B200 library that need no GPU.
 
-* the C-ABI libraries load and export every entry point include/awa_b200.h declares;
+* the C-ABI libraries load and export every entry point include/*.h declares;
 * the window rule and every index map of a plan are bit-identical to the oracle
   (which is itself pinned to the reference);
 * load_param's error behaviour (invalid params, -1,-1,-1 grid with/without a
@@ -19,12 +19,12 @@ import awa_b200
 from oracle.oracle import LayerConfig
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADER = os.path.join(ROOT, "include", "awa_b200.h")
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("awa_b200.h", "awa_package.h")]
 GOLDEN = os.path.join(ROOT, "tests", "golden")
 
 
 def declared_functions():
-    text = open(HEADER).read()
+    text = "".join(open(h).read() for h in HEADERS)
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     return sorted(set(re.findall(r"\b(awa_\w+)\s*\(", text)))
 
