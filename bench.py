@@ -521,6 +521,148 @@ def run_qkv_proj(args, rank, world, local_rank):
     }
 
 
+STACK_BLOCKS, STACK_FP32_BLOCKS = 32, 9
+
+
+def run_stack(args, rank, world, local_rank):
+    """--stage stack: the attention path of a 32-block DiT step through the
+    block-stack driver (awa_stack): per block the QKV projection with Q/K
+    RMSNorm, the AWA chain (fp32 in the first 9 blocks, bf16 after, odd blocks
+    shifted) and proj_out + gate + residual, the residual stream carried from
+    block to block. Timed three ways: with a host wait after every block (the
+    reference's submit-and-wait per block), on one stream with no wait, and as
+    one CUDA graph. A step is one 32-block pass; inputs resident in HBM."""
+    import torch
+    import torch.distributed as dist
+
+    import awa_b200
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    grid, num, _, _, _ = WORKLOADS[args.workload]
+    n_v = grid[0] * grid[1] * grid[2]
+    lib = awa_b200.library()
+    gen = torch.Generator(device=device).manual_seed(99 + rank)
+
+    def rnd(*shape, scale=1.0):
+        return torch.randn(*shape, device=device, generator=gen) * scale
+
+    sets = [{"wqkv": rnd(3 * MODEL_DIM, MODEL_DIM, scale=MODEL_DIM ** -0.5).bfloat16(),
+             "wout": rnd(MODEL_DIM, MODEL_DIM, scale=MODEL_DIM ** -0.5).bfloat16(),
+             "gq": 1.0 + 0.2 * rnd(HEAD_DIM), "gk": 1.0 + 0.2 * rnd(HEAD_DIM),
+             "bias": 0.02 * rnd(MODEL_DIM), "gate": 0.1 * rnd(MODEL_DIM)} for _ in range(4)]
+    x0, t0 = rnd(n_v, MODEL_DIM).bfloat16(), rnd(TEXT, MODEL_DIM).bfloat16()
+    xv = [torch.empty_like(x0) for _ in range(2)]
+    xt = [torch.empty_like(t0) for _ in range(2)]
+    qkv = {dt: (torch.empty(n_v, 3, HEADS, HEAD_DIM, device=device, dtype=dt),
+                torch.empty(TEXT, 3, HEADS, HEAD_DIM, device=device, dtype=dt))
+           for dt in (torch.float32, torch.bfloat16)}
+    attn_v = torch.empty(n_v, MODEL_DIM, device=device, dtype=torch.bfloat16)
+    attn_t = torch.empty(TEXT, MODEL_DIM, device=device, dtype=torch.bfloat16)
+    state = {"cur": 0, "sync": False}
+    dim = MODEL_DIM
+
+    def hook(stage, io, handle):
+        w, cur = sets[io.block % 4], state["cur"]
+        if stage == awa_b200.AWA_STACK_BEFORE:
+            fp32 = io.precision == awa_b200.AWA_PREC_FP32
+            qv, qt = qkv[torch.float32 if fp32 else torch.bfloat16]
+            code = awa_b200.AWA_F32 if fp32 else awa_b200.AWA_BF16
+            for x, q, rows in ((xv[cur], qv, n_v), (xt[cur], qt, TEXT)):
+                if lib.awa_qkv_project(rows, dim, HEADS, HEAD_DIM, x.data_ptr(), dim, w["wqkv"].data_ptr(), dim,
+                                       w["gq"].data_ptr(), w["gk"].data_ptr(), 1e-5, code, q.data_ptr(), 3 * dim,
+                                       handle):
+                    return 1
+            io.in_dtype = code
+            io.video_qkv, io.video_token_stride, io.video_qkv_stride = qv.data_ptr(), 3 * dim, dim
+            io.text_qkv, io.text_token_stride, io.text_qkv_stride = qt.data_ptr(), 3 * dim, dim
+            io.out_dtype = awa_b200.AWA_BF16
+            io.video_out, io.video_out_stride = attn_v.data_ptr(), dim
+            io.text_out, io.text_out_stride = attn_t.data_ptr(), dim
+            return 0
+        nxt = 1 - cur
+        for a, x, y, rows in ((attn_v, xv[cur], xv[nxt], n_v), (attn_t, xt[cur], xt[nxt], TEXT)):
+            if lib.awa_out_project(rows, dim, dim, a.data_ptr(), dim, w["wout"].data_ptr(), dim, w["bias"].data_ptr(),
+                                   w["gate"].data_ptr(), x.data_ptr(), dim, awa_b200.AWA_BF16, awa_b200.AWA_BF16,
+                                   y.data_ptr(), dim, handle):
+                return 1
+        state["cur"] = nxt
+        if state["sync"]:
+            stream.synchronize()  # the reference waits for every block on the host
+        return 0
+
+    params = [{"source_t": -1, "source_h": -1, "source_w": -1, "windows_t": num[0], "windows_h": num[1],
+               "windows_w": num[2], "text_tokens": TEXT, "shifted": b % 2, "rope_dim": 126}
+              for b in range(STACK_BLOCKS)]
+    stack = awa_b200.AwaStack(params, runtime_spec=grid, fp32_blocks=STACK_FP32_BLOCKS, heads=HEADS,
+                              head_dim=HEAD_DIM)
+    stream = torch.cuda.Stream(device)
+
+    def reset():
+        xv[0].copy_(x0)
+        xt[0].copy_(t0)
+        state["cur"] = 0
+
+    with torch.cuda.stream(stream):
+        reset()
+        stack.run(hook, stream)
+        reset()
+        graph = stack.capture(hook, stream)
+    stream.synchronize()
+    awa_b200.device_status()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def timed(mode):
+        state["sync"] = mode == "host_sync"
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                reset()
+                graph.launch(stream) if mode == "graph" else stack.run(hook, stream)
+        stream.synchronize()
+        barrier()
+        total = 0.0
+        for _ in range(args.steps):
+            with torch.cuda.stream(stream):
+                reset()
+                start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record(stream)
+                graph.launch(stream) if mode == "graph" else stack.run(hook, stream)
+                stop.record(stream)
+            stop.synchronize()
+            total += start.elapsed_time(stop)
+        barrier()
+        state["sync"] = False
+        return total / args.steps
+
+    clocks = ClockSampler(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                          int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank]))
+    ms = {mode: timed(mode) for mode in ("host_sync", "stream", "graph")}
+    clock = clocks.stop()
+    awa_b200.device_status()
+    if world > 1:
+        t = torch.tensor([ms["graph"]], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms["graph"] = float(t.item())
+    del graph
+    plans, ws = stack.info()
+    return {
+        "metric": "DiT step attention path (32 blocks: QKV proj + RMSNorm, AWA, proj_out + gate + residual) ms",
+        "value": round(ms["graph"], 4), "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms["graph"], 4), "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 (fp32 in blocks 0-8)", "data": "synthetic residual stream, random weights",
+        "config": {"workload": f"{args.workload}-stack", "grid": list(grid), "num_windows": list(num),
+                   "blocks": STACK_BLOCKS, "fp32_blocks": STACK_FP32_BLOCKS, "plans": plans,
+                   "workspace_bytes": ws},
+        "modes_ms": {k: round(v, 4) for k, v in ms.items()},
+        # per block: 2 QKV projections, attention + text mean, 2 output projections; 3 timed modes
+        "gpu_launches": STACK_BLOCKS * 6 * args.steps * 3,
+        "clocks": clock,
+    }
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -531,9 +673,9 @@ def main():
     parser.add_argument("--e2e-steps", type=int, default=20)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiler captures)")
-    parser.add_argument("--stage", default="awa", choices=["awa", "qkv-proj", "out-proj"],
+    parser.add_argument("--stage", default="awa", choices=["awa", "qkv-proj", "out-proj", "stack"],
                         help="awa: the AWA layer (the headline); qkv-proj / out-proj: its input's producer / "
-                             "its output's consumer")
+                             "its output's consumer; stack: the attention path of 32 blocks via the stack driver")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
@@ -557,8 +699,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.stage in ("qkv-proj", "out-proj"):
-            line = run_qkv_proj(args, rank, world, local_rank)
+        if args.stage in ("qkv-proj", "out-proj", "stack"):
+            line = (run_stack if args.stage == "stack" else run_qkv_proj)(args, rank, world, local_rank)
             if rank == 0:
                 print(json.dumps(line), flush=True)
             return

@@ -32,7 +32,7 @@ AWA_ERR_DEVICE = -3
 AWA_ERR_ALLOC = -100
 AWA_NOALLOC_SCRATCH_BYTES = 32 << 20  # scratch of awa_forward_noalloc, per GPU
 
-# Every symbol declared in include/awa_b200.h and include/awa_package.h.
+# Every symbol declared in include/awa_b200.h, include/awa_package.h and include/awa_stack.h.
 EXPORTED_SYMBOLS = (
     "awa_make_windows", "awa_plan_create", "awa_plan_create_host", "awa_plan_destroy", "awa_plan_get_info", "awa_plan_get_maps",
     "awa_pack", "awa_mmrope", "awa_window_attention", "awa_unpack", "awa_forward_workspace_bytes", "awa_forward",
@@ -43,6 +43,8 @@ EXPORTED_SYMBOLS = (
     "awa_profile_enable", "awa_profile_reset", "awa_profile_collect", "awa_last_error", "awa_version",
     "awa_graph_find_chains", "awa_graph_find_chains_file", "awa_graph_make_dynamic", "awa_manifest_validate",
     "awa_sha256", "awa_sha256_file",
+    "awa_stack_create", "awa_stack_destroy", "awa_stack_get_info", "awa_stack_block_plan", "awa_stack_forward_block",
+    "awa_stack_run", "awa_stack_capture", "awa_stack_graph_launch", "awa_stack_graph_destroy",
 )
 
 
@@ -68,6 +70,22 @@ class _Window(ctypes.Structure):
 class _GraphChain(ctypes.Structure):
     _fields_ = [("params", _LayerParams)] + [(n, ctypes.c_int) for n in (
         "dynamic", "pack_line", "rope_line", "attention_line", "unpack_line", "reshape_line", "reshape_height")]
+
+
+class StackIO(ctypes.Structure):
+    """awa_stack_io: one block's AWA input and output (include/awa_stack.h)."""
+    _fields_ = [("block", ctypes.c_int), ("precision", ctypes.c_int), ("in_dtype", ctypes.c_int),
+                ("video_qkv", ctypes.c_void_p), ("video_token_stride", ctypes.c_int64),
+                ("video_qkv_stride", ctypes.c_int64), ("text_qkv", ctypes.c_void_p),
+                ("text_token_stride", ctypes.c_int64), ("text_qkv_stride", ctypes.c_int64),
+                ("out_dtype", ctypes.c_int), ("video_out", ctypes.c_void_p), ("video_out_stride", ctypes.c_int64),
+                ("text_out", ctypes.c_void_p), ("text_out_stride", ctypes.c_int64)]
+
+
+# int (*awa_stack_hook)(void* user, int stage, awa_stack_io* io, awa_stream_t stream)
+STACK_HOOK = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(StackIO), ctypes.c_void_p)
+AWA_STACK_BEFORE = 0
+AWA_STACK_AFTER = 1
 
 
 class _PlanInfo(ctypes.Structure):
@@ -123,6 +141,15 @@ def library() -> ctypes.CDLL:
         "awa_manifest_validate": (i, [ctypes.c_char_p, i]),
         "awa_sha256": (i, [ctypes.c_char_p, sz, p]),
         "awa_sha256_file": (i, [ctypes.c_char_p, p]),
+        "awa_stack_create": (i, [p, i, p, i, i, i, ctypes.POINTER(p)]),
+        "awa_stack_destroy": (None, [p]),
+        "awa_stack_get_info": (i, [p, p, p]),
+        "awa_stack_block_plan": (p, [p, i]),
+        "awa_stack_forward_block": (i, [p, i, p, p]),
+        "awa_stack_run": (i, [p, STACK_HOOK, p, p]),
+        "awa_stack_capture": (i, [p, STACK_HOOK, p, p, ctypes.POINTER(p)]),
+        "awa_stack_graph_launch": (i, [p, p]),
+        "awa_stack_graph_destroy": (None, [p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -408,6 +435,93 @@ def out_project(x, w, bias, gate, residual, out_dtype=None, out=None, stream=Non
     return out
 
 
+class AwaStack:
+    """The AWA chains of a DiT block stack on one stream (include/awa_stack.h).
+
+    block_params: one dict of awa_layer_params fields per block (e.g. the
+    "params" of graph_find_chains for each block graph); fp32_blocks leading
+    blocks run in fp32, the rest in bf16. Built on the current device.
+    """
+
+    def __init__(self, block_params, runtime_spec=None, fp32_blocks: int = 0, heads: int = 20, head_dim: int = 128):
+        lib = library()
+        arr = (_LayerParams * len(block_params))()
+        for i, p in enumerate(block_params):
+            arr[i] = _LayerParams(*(int(p.get(f, 126 if f == "rope_dim" else 0)) for f, _ in _LayerParams._fields_))
+        spec = None
+        if runtime_spec is not None:
+            t, h, w = runtime_spec
+            spec = _RuntimeSpec(t, h, w, t * h * w)
+        handle = ctypes.c_void_p()
+        _check(lib.awa_stack_create(ctypes.cast(arr, ctypes.c_void_p), len(block_params),
+                                    ctypes.byref(spec) if spec is not None else None, int(fp32_blocks), int(heads),
+                                    int(head_dim), ctypes.byref(handle)))
+        self._handle = handle
+        self.blocks = len(block_params)
+
+    def __del__(self):
+        handle = getattr(self, "_handle", None)
+        if handle and _lib is not None:
+            _lib.awa_stack_destroy(handle)
+            self._handle = None
+
+    @property
+    def handle(self):
+        return self._handle
+
+    def info(self) -> Tuple[int, int]:
+        """(distinct plans, workspace bytes)."""
+        plans, ws = ctypes.c_int(0), ctypes.c_size_t(0)
+        _check(library().awa_stack_get_info(self._handle, ctypes.byref(plans), ctypes.byref(ws)))
+        return plans.value, ws.value
+
+    def _callback(self, hook, errors):
+        def call(_user, stage, io, stream):
+            try:
+                return int(hook(stage, io.contents, stream) or 0)
+            except BaseException as exc:  # reported after the C call returns
+                errors.append(exc)
+                return 1
+        return STACK_HOOK(call)
+
+    def run(self, hook, stream) -> None:
+        """hook(stage, io: StackIO, stream_handle) enqueues the caller's work
+        on the raw stream handle and fills io at AWA_STACK_BEFORE."""
+        errors = []
+        cb = self._callback(hook, errors)
+        rc = library().awa_stack_run(self._handle, cb, None, _stream_ptr(stream))
+        if errors:
+            raise errors[0]
+        _check(rc)
+
+    def capture(self, hook, stream) -> "StackGraph":
+        """run() captured into a CUDA graph on stream (not the default stream)."""
+        errors = []
+        cb = self._callback(hook, errors)
+        graph = ctypes.c_void_p()
+        rc = library().awa_stack_capture(self._handle, cb, None, _stream_ptr(stream), ctypes.byref(graph))
+        if errors:
+            raise errors[0]
+        _check(rc)
+        return StackGraph(graph)
+
+
+class StackGraph:
+    """An instantiated CUDA graph of one stack run (awa_stack_capture)."""
+
+    def __init__(self, handle):
+        self._handle = handle
+
+    def launch(self, stream) -> None:
+        _check(library().awa_stack_graph_launch(self._handle, _stream_ptr(stream)))
+
+    def __del__(self):
+        handle = getattr(self, "_handle", None)
+        if handle and _lib is not None:
+            _lib.awa_stack_graph_destroy(handle)
+            self._handle = None
+
+
 def device_status() -> None:
     """Raise if a device-side check of the library failed since the last call."""
     _check(library().awa_device_status())
@@ -552,4 +666,5 @@ def sha256_file(path) -> str:
 
 __all__ = ["AwaPlan", "AwaError", "PlanInfo", "library", "make_windows", "device_status", "ncnn_run_chain",
            "EXPORTED_SYMBOLS", "qkv_project", "out_project", "graph_find_chains", "graph_find_chains_file",
-           "graph_make_dynamic", "manifest_validate", "sha256", "sha256_file", "AWA_F32", "AWA_BF16", "AWA_PREC_FP32", "AWA_PREC_BF16"]
+           "graph_make_dynamic", "manifest_validate", "sha256", "sha256_file", "AwaStack", "StackGraph", "StackIO",
+           "AWA_STACK_BEFORE", "AWA_STACK_AFTER", "AWA_F32", "AWA_BF16", "AWA_PREC_FP32", "AWA_PREC_BF16"]

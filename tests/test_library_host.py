@@ -19,7 +19,7 @@ import awa_b200
 from oracle.oracle import LayerConfig
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADERS = [os.path.join(ROOT, "include", h) for h in ("awa_b200.h", "awa_package.h")]
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("awa_b200.h", "awa_package.h", "awa_stack.h")]
 GOLDEN = os.path.join(ROOT, "tests", "golden")
 
 
