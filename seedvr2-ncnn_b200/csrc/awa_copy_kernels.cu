@@ -283,11 +283,25 @@ __device__ __forceinline__ float2 load_pair_cs(const __nv_bfloat16* p)
     return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
 }
 
+// One pair of partials as loaded (raw bits), widened to fp32 when summed.
+__device__ __forceinline__ float2 raw_pair_cs(const float* p) { return load_pair_cs(p); }
+__device__ __forceinline__ uint32_t raw_pair_cs(const __nv_bfloat16* p)
+{
+    return __ldcs(reinterpret_cast<const unsigned int*>(p));
+}
+__device__ __forceinline__ float2 widen_pair(float2 x) { return x; }
+__device__ __forceinline__ float2 widen_pair(uint32_t w)
+{
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
 // text_reduce for dense partials ([W][text][head_row] rows of fp32 or bf16)
 // whose rows and base are aligned to two elements: two consecutive elements
-// per thread, sixteen windows in flight per thread (more threads in flight
-// than with 16-byte loads, which measured slower); the sum in window order,
-// then / divisor (as text_reduce does for dense partials).
+// per thread (more threads in flight than with 16-byte loads, which measured
+// slower). Each thread's windows are a serial chain of load batches, so the
+// batch is as deep as registers allow (48 bf16 or 24 fp32 pairs in flight);
+// the sum in window order, then / divisor (as text_reduce does for dense
+// partials).
 template <typename TIn, typename TOut>
 __global__ void text_reduce_v2(int text, int head_row, const TIn* __restrict__ src, int64_t sts, int windows,
                                float divisor, TOut* __restrict__ out, int64_t ots)
@@ -301,20 +315,21 @@ __global__ void text_reduce_v2(int text, int head_row, const TIn* __restrict__ s
         const int e = (int)(id - (int64_t)i * pairs) * 2;
         const TIn* col = src + (int64_t)i * sts + e;
         const int64_t wstride = (int64_t)text * sts;  // one window's text rows
-        constexpr int kBatch = 16;
+        constexpr int kBatch = sizeof(TIn) == 2 ? 48 : 24;
         float2 acc = make_float2(0.f, 0.f);
         int w = 0;
         for (; w + kBatch <= windows; w += kBatch)
         {
-            float2 x[kBatch];
+            decltype(raw_pair_cs(col)) x[kBatch];
 #pragma unroll
             for (int u = 0; u < kBatch; u++)
-                x[u] = load_pair_cs(col + (int64_t)(w + u) * wstride);
+                x[u] = raw_pair_cs(col + (int64_t)(w + u) * wstride);
 #pragma unroll
             for (int u = 0; u < kBatch; u++)
             {
-                acc.x = __fadd_rn(acc.x, x[u].x);
-                acc.y = __fadd_rn(acc.y, x[u].y);
+                const float2 v = widen_pair(x[u]);
+                acc.x = __fadd_rn(acc.x, v.x);
+                acc.y = __fadd_rn(acc.y, v.y);
             }
         }
         for (; w < windows; w++)
