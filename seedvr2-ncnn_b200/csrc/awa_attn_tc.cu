@@ -406,14 +406,14 @@ __device__ __forceinline__ bool warp_all(bool ok)
 }
 
 // ---------------------------------------------------------------- RoPE in bf16x2
-// Rotate one bf16 pair (x0 low, x1 high) by the table entry t = (cos low, sin
-// high): (x0 c - x1 s, x1 c + x0 s) = w * (c, c) + swap(w) * (-s, s).
-__device__ __forceinline__ uint32_t rotate_bf16x2(uint32_t w, uint32_t t)
+// Rotate one bf16 pair (x0 low, x1 high) by the table entry f = ((cos, cos),
+// (-sin, sin)): (x0 c - x1 s, x1 c + x0 s) = w * (c, c) + swap(w) * (-s, s).
+// The table holds the two factor words ready, so a pair costs one 8-byte load
+// and three instructions.
+__device__ __forceinline__ uint32_t rotate_bf16x2(uint32_t w, uint2 f)
 {
-    uint32_t cc, ns, prod, sw, out;
-    asm("prmt.b32 %0, %1, %1, 0x1010;" : "=r"(cc) : "r"(t));
-    asm("prmt.b32 %0, %1, %1, 0x3232;" : "=r"(ns) : "r"(t));
-    ns ^= 0x00008000u;  // negate the low half: (-s, s)
+    const uint32_t cc = f.x, ns = f.y;
+    uint32_t prod, sw, out;
     asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(prod) : "r"(w), "r"(cc));
     asm("prmt.b32 %0, %1, %1, 0x1032;" : "=r"(sw) : "r"(w));
     asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(out) : "r"(sw), "r"(ns), "r"(prod));
@@ -434,24 +434,29 @@ __device__ __forceinline__ uint32_t swizzled_offset(int rows, int r, int c)
 // pair p on axis x is base[x] + p. Pairs at or past rope_dim / 2 pass
 // through. With RD != 0, the axis of every pair is a compile-time constant.
 template <int HALF, int RD>
-__device__ __forceinline__ void rotate_half_row(uint32_t (&words)[32], const int (&base)[3], const uint32_t* table,
+__device__ __forceinline__ void rotate_half_row(uint32_t (&words)[32], const int (&base)[3], const uint2* table,
                                                 int ppa_rt, int rope_dim_rt)
 {
     const int ppa = RD ? RD / 6 : ppa_rt;
     const int rope_dim = RD ? RD : rope_dim_rt;
-    uint32_t cs[32];
 #pragma unroll
-    for (int k = 0; k < 32; k++)
+    for (int batch = 0; batch < 2; batch++)  // 16 pairs' factors (32 registers) at a time
     {
-        const int pair = 32 * HALF + k;  // features 2 pair, 2 pair + 1
-        const int b = pair < ppa ? base[0] : pair < 2 * ppa ? base[1] : base[2];
-        cs[k] = __ldg(table + (2 * pair < rope_dim ? b + pair : 0));
-    }
+        uint2 f[16];
 #pragma unroll
-    for (int k = 0; k < 32; k++)
-    {
-        const uint32_t rotated = rotate_bf16x2(words[k], cs[k]);
-        words[k] = 2 * (32 * HALF + k) < rope_dim ? rotated : words[k];
+        for (int k = 0; k < 16; k++)
+        {
+            const int pair = 32 * HALF + 16 * batch + k;  // features 2 pair, 2 pair + 1
+            const int b = pair < ppa ? base[0] : pair < 2 * ppa ? base[1] : base[2];
+            f[k] = __ldg(table + (2 * pair < rope_dim ? b + pair : 0));
+        }
+#pragma unroll
+        for (int k = 0; k < 16; k++)
+        {
+            const int w = 16 * batch + k;
+            const uint32_t rotated = rotate_bf16x2(words[w], f[k]);
+            words[w] = 2 * (32 * HALF + w) < rope_dim ? rotated : words[w];
+        }
     }
 }
 
@@ -630,7 +635,7 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
     const int ppa = RD ? RD / 6 : a.plan.pairs_per_axis;
     const int rope_dim = RD ? RD : a.plan.rope_dim;
     const int bwc = a.plan.tc_bwc > 0 ? a.plan.tc_bwc : 1;
-    const uint32_t* table = a.plan.rope_table_bf16;  // read through L1
+    const uint2* table = a.plan.rope_factors_bf16;  // read through L1
     volatile int* abort = &sh.abort;
     uint32_t q_loaded_phase = 0;
     uint32_t q_empty_phase = 1;  // TMEM Q starts free

@@ -32,7 +32,7 @@ struct awa_plan
     std::vector<int> video_positions;
     std::vector<int> text_positions;
     std::vector<float2> rope_table;
-    std::vector<uint32_t> rope_table_bf16;  // per (coord, pair): bf16 cos (low half), bf16 sin (high half)
+    std::vector<uint2> rope_factors_bf16;  // per (coord, pair): bf16x2 (cos, cos), bf16x2 (-sin, sin)
     std::vector<short4> position_coords;
     std::vector<int2> items_tc;         // fused tcgen05 path: (window, pair of 128-row q tiles), longest first
     std::vector<int2> items_tc_packed;  // packed tcgen05 path: same, over the packed rows
@@ -360,7 +360,7 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
     plan->max_coord = max_coord;
     const int axis_dim = rope_dim / 3;
     plan->rope_table.resize((size_t)max_coord * plan->pairs_per_axis);
-    plan->rope_table_bf16.resize(plan->rope_table.size());
+    plan->rope_factors_bf16.resize(plan->rope_table.size());
     for (int pair = 0; pair < plan->pairs_per_axis; pair++)
     {
         const float frequency = std::pow(10000.f, -static_cast<float>(2 * pair) / axis_dim);
@@ -369,7 +369,12 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
             const float angle = coord * frequency;
             const float c = std::cos(angle), sn = std::sin(angle);
             plan->rope_table[(size_t)coord * plan->pairs_per_axis + pair] = make_float2(c, sn);
-            plan->rope_table_bf16[(size_t)coord * plan->pairs_per_axis + pair] = bf16_pair(c, sn);
+            // the tensor-core kernel's rotation factors of the same entry, in bf16:
+            // x' = x c - y s, y' = y c + x s as (x, y) * (c, c) + (y, x) * (-s, s)
+            const uint32_t cs = bf16_pair(c, sn);
+            const uint32_t cc = (cs & 0xffffu) | (cs << 16);
+            const uint32_t ns = ((cs >> 16) | (cs & 0xffff0000u)) ^ 0x8000u;
+            plan->rope_factors_bf16[(size_t)coord * plan->pairs_per_axis + pair] = make_uint2(cc, ns);
         }
     }
 
@@ -457,7 +462,7 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
     const size_t sizes[kSegments] = {
         bytes_of(plan->descs),           bytes_of(plan->sequence_index), bytes_of(plan->cu_seqlens),
         bytes_of(plan->video_positions), bytes_of(plan->position_coords), bytes_of(plan->rope_table),
-        bytes_of(plan->items_tc),        bytes_of(plan->items_simt),      bytes_of(plan->rope_table_bf16),
+        bytes_of(plan->items_tc),        bytes_of(plan->items_simt),      bytes_of(plan->rope_factors_bf16),
         bytes_of(plan->items_tc_packed)};
     for (int i = 0; i < kSegments; i++)
     {
@@ -474,7 +479,7 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
     const void* sources[kSegments] = {
         plan->descs.data(),           plan->sequence_index.data(),  plan->cu_seqlens.data(),
         plan->video_positions.data(), plan->position_coords.data(), plan->rope_table.data(),
-        plan->items_tc.data(),        plan->items_simt.data(),      plan->rope_table_bf16.data(),
+        plan->items_tc.data(),        plan->items_simt.data(),      plan->rope_factors_bf16.data(),
         plan->items_tc_packed.data()};
     for (int i = 0; i < kSegments; i++)
         if (sizes[i])
@@ -494,7 +499,7 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
     dev.video_positions = reinterpret_cast<const int*>(base + offsets[3]);
     dev.position_coords = reinterpret_cast<const int*>(base + offsets[4]);
     dev.rope_table = reinterpret_cast<const float2*>(base + offsets[5]);
-    dev.rope_table_bf16 = reinterpret_cast<const uint32_t*>(base + offsets[8]);
+    dev.rope_factors_bf16 = reinterpret_cast<const uint2*>(base + offsets[8]);
     plan->d_items_tc = reinterpret_cast<const int2*>(base + offsets[6]);
     plan->d_items_simt = reinterpret_cast<const int2*>(base + offsets[7]);
     plan->d_items_tc_packed = reinterpret_cast<const int2*>(base + offsets[9]);
