@@ -429,10 +429,23 @@ __device__ __forceinline__ uint32_t swizzled_offset(int rows, int r, int c)
     return (uint32_t)((c >> 3) * rows * 128 + r * 128 + ((((c & 7) ^ (r & 7))) << 4));
 }
 
+// Whether the factors of `pair` and the next pair load as one 16-byte vector:
+// both rotated, on one axis, the first at an even index within its axis (the
+// factor rows have even length), and in the same batch of 16. Compile-time
+// when RD != 0.
+template <int RD>
+__device__ __forceinline__ bool factors_paired(int pair, int k, int ppa, int rope_dim)
+{
+    const int axis = pair < ppa ? 0 : pair < 2 * ppa ? 1 : 2;
+    const int q = pair - axis * ppa;
+    return RD != 0 && k + 1 < 16 && (q & 1) == 0 && q + 1 < ppa && 2 * (pair + 1) < rope_dim;
+}
+
 // Rotate 32 consecutive bf16 pairs (half a 128-feature row: pairs 32*HALF ..)
-// of one row whose table bases are base[x] = (coord_x - x) * ppa: the entry of
-// pair p on axis x is base[x] + p. Pairs at or past rope_dim / 2 pass
-// through. With RD != 0, the axis of every pair is a compile-time constant.
+// of one row whose table bases are base[x] = coord_x * stride - x * ppa (stride
+// = ppa rounded up to even): the factors of pair p on axis x are at
+// base[x] + p. Pairs at or past rope_dim / 2 pass through. With RD != 0, the
+// axis of every pair is a compile-time constant.
 template <int HALF, int RD>
 __device__ __forceinline__ void rotate_half_row(uint32_t (&words)[32], const int (&base)[3], const uint2* table,
                                                 int ppa_rt, int rope_dim_rt)
@@ -448,7 +461,16 @@ __device__ __forceinline__ void rotate_half_row(uint32_t (&words)[32], const int
         {
             const int pair = 32 * HALF + 16 * batch + k;  // features 2 pair, 2 pair + 1
             const int b = pair < ppa ? base[0] : pair < 2 * ppa ? base[1] : base[2];
-            f[k] = __ldg(table + (2 * pair < rope_dim ? b + pair : 0));
+            if (k > 0 && factors_paired<RD>(pair - 1, k - 1, ppa, rope_dim))
+                continue;  // loaded with the previous pair
+            if (factors_paired<RD>(pair, k, ppa, rope_dim))
+            {
+                const uint4 v = __ldg(reinterpret_cast<const uint4*>(table + b + pair));
+                f[k] = make_uint2(v.x, v.y);
+                f[k + 1] = make_uint2(v.z, v.w);
+            }
+            else
+                f[k] = __ldg(table + (2 * pair < rope_dim ? b + pair : 0));
         }
 #pragma unroll
         for (int k = 0; k < 16; k++)
@@ -465,6 +487,7 @@ __device__ __forceinline__ void rotate_half_row(uint32_t (&words)[32], const int
 __device__ __forceinline__ void row_bases(int (&base)[3], bool valid, const BlockGeo& geo, int text, int row_h,
                                           int row_w, int hoff, int woff, int row, int ppa)
 {
+    const int stride = ppa + (ppa & 1);
     int ct = 0, ch = 1, cw = 2;
     if (valid)
     {
@@ -477,9 +500,9 @@ __device__ __forceinline__ void row_bases(int (&base)[3], bool valid, const Bloc
         else
             ct = ch = cw = geo.first + row;
     }
-    base[0] = ct * ppa;
-    base[1] = (ch - 1) * ppa;
-    base[2] = (cw - 2) * ppa;
+    base[0] = ct * stride;
+    base[1] = ch * stride - ppa;
+    base[2] = cw * stride - 2 * ppa;
 }
 
 __device__ __forceinline__ void load_half_row(uint32_t (&words)[32], const uint8_t* tile, int rows, int r, int half)

@@ -31,7 +31,8 @@ struct PlanDevice
     const int* video_positions = nullptr;  // [N_v]
     const int* position_coords = nullptr;  // [S] short4 RoPE coordinates (t, h, w, 0) per packed row
     const float2* rope_table = nullptr;    // [max_coord][pairs_per_axis] (cos, sin)
-    const uint2* rope_factors_bf16 = nullptr;  // same entries as bf16x2 words (cos, cos), (-sin, sin)
+    const uint2* rope_factors_bf16 = nullptr;  // same entries as bf16x2 words (cos, cos), (-sin, sin),
+                                               // rows of pairs_per_axis rounded up to even
     int source_t = 0, source_h = 0, source_w = 0;
     int source_tokens = 0;
     int text_tokens = 0;

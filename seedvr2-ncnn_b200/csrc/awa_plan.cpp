@@ -360,7 +360,10 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
     plan->max_coord = max_coord;
     const int axis_dim = rope_dim / 3;
     plan->rope_table.resize((size_t)max_coord * plan->pairs_per_axis);
-    plan->rope_factors_bf16.resize(plan->rope_table.size());
+    // factor rows padded to an even length, so two pairs of one axis starting at
+    // an even pair load as one 16-byte vector
+    const int factor_stride = plan->pairs_per_axis + (plan->pairs_per_axis & 1);
+    plan->rope_factors_bf16.assign((size_t)max_coord * factor_stride, make_uint2(0u, 0u));
     for (int pair = 0; pair < plan->pairs_per_axis; pair++)
     {
         const float frequency = std::pow(10000.f, -static_cast<float>(2 * pair) / axis_dim);
@@ -374,7 +377,7 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
             const uint32_t cs = bf16_pair(c, sn);
             const uint32_t cc = (cs & 0xffffu) | (cs << 16);
             const uint32_t ns = ((cs >> 16) | (cs & 0xffff0000u)) ^ 0x8000u;
-            plan->rope_factors_bf16[(size_t)coord * plan->pairs_per_axis + pair] = make_uint2(cc, ns);
+            plan->rope_factors_bf16[(size_t)coord * factor_stride + pair] = make_uint2(cc, ns);
         }
     }
 
