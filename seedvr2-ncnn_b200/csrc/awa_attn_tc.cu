@@ -868,6 +868,52 @@ __device__ void mma_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t tm
     drain_bar(&sh.bar.mma_done, 0, a.error_flag, 26);
 }
 
+// ---------------------------------------------------------------- packed fp32 helpers
+// sm_100 executes two fp32 lanes per instruction for add / mul / fma on
+// register pairs (.f32x2) and takes three operands in max.f32: the softmax's
+// arithmetic is bound by the FMA-pipe issue it shares with the RoPE warps, so
+// it uses those forms. Each lane rounds as the scalar instruction does.
+__device__ __forceinline__ void fma_x2(float& d0, float& d1, float a0, float a1, float b, float c)
+{
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %4};\n\t"
+        "mov.b64 rc, {%5, %5};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+
+__device__ __forceinline__ void add_x2(float& acc0, float& acc1, float a0, float a1)
+{
+    asm("{\n\t.reg .b64 ra, rb;\n\t"
+        "mov.b64 ra, {%0, %1};\n\t"
+        "mov.b64 rb, {%2, %3};\n\t"
+        "add.rn.f32x2 ra, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, ra;\n\t}"
+        : "+f"(acc0), "+f"(acc1)
+        : "f"(a0), "f"(a1));
+}
+
+__device__ __forceinline__ void mul_x2(float& d0, float& d1, float a0, float a1, float b)
+{
+    asm("{\n\t.reg .b64 ra, rb;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %4};\n\t"
+        "mul.rn.f32x2 ra, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, ra;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b));
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 // ---------------------------------------------------------------- softmax + epilogue
 template <bool PACKED, typename TOut>
 __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t tmem)
@@ -949,15 +995,14 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
                     if (!((mask >> i) & 1ull))
                         v[i] = 0xff800000u;  // -inf: p = 0
             }
-            float mxp[8];
+            float mxp[4];
 #pragma unroll
-            for (int i = 0; i < 8; i++)
+            for (int i = 0; i < 4; i++)
                 mxp[i] = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < 64; i++)
-                mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(v[i]));
-            const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                                   fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+            for (int i = 0; i < 32; i++)
+                mxp[i & 3] = max3(mxp[i & 3], __uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+            const float mx = max3(max3(mxp[0], mxp[1], mxp[2]), mxp[3], -INFINITY);
             const float m_blk = mx * scale_log2;
             float alpha = 1.f;
             bool rescale = false;
@@ -981,15 +1026,20 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
                     tc::tmem_ld16(t_o + cc * 16, o);
                     tc::tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 16; i++)
-                        o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    for (int i = 0; i < 16; i += 2)
+                    {
+                        float a0, a1;
+                        mul_x2(a0, a1, __uint_as_float(o[i]), __uint_as_float(o[i + 1]), alpha);
+                        o[i] = __float_as_uint(a0);
+                        o[i + 1] = __float_as_uint(a1);
+                    }
                     tc::tmem_st16(t_o + cc * 16, o);
                 }
             }
             // P = exp2(s * scale - max), rounded to bf16, two keys per column, over S.
             // (No key seen yet: m_run = -inf and every p is 0.)
             const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
-            float sums[4] = {0.f, 0.f, 0.f, 0.f};
+            float sums[4] = {0.f, 0.f, 0.f, 0.f};  // two lane pairs
 #pragma unroll
             for (int h = 0; h < 2; h++)
             {
@@ -998,9 +1048,11 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
                 for (int i = 0; i < 16; i++)
                 {
                     const int k = 32 * h + 2 * i;
-                    const float p0 = fast_exp2(fmaf(__uint_as_float(v[k]), scale_log2, neg_m));
-                    const float p1 = fast_exp2(fmaf(__uint_as_float(v[k + 1]), scale_log2, neg_m));
-                    sums[i & 3] += p0 + p1;
+                    float x0, x1;
+                    fma_x2(x0, x1, __uint_as_float(v[k]), __uint_as_float(v[k + 1]), scale_log2, neg_m);
+                    const float p0 = fast_exp2(x0);
+                    const float p1 = fast_exp2(x1);
+                    add_x2(sums[2 * (i & 1)], sums[2 * (i & 1) + 1], p0, p1);
                     pk[i] = pack_bf16x2(p0, p1);
                 }
                 tc::tmem_st16(t_s + 16 * h, pk);
@@ -1036,8 +1088,13 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
                 if (f32)
                 {
 #pragma unroll
-                    for (int i = 0; i < 64; i++)
-                        o[i] = __float_as_uint(__uint_as_float(o[i]) * inv);
+                    for (int i = 0; i < 64; i += 2)
+                    {
+                        float a0, a1;
+                        mul_x2(a0, a1, __uint_as_float(o[i]), __uint_as_float(o[i + 1]), inv);
+                        o[i] = __float_as_uint(a0);
+                        o[i + 1] = __float_as_uint(a1);
+                    }
                     if (a.out_v8)
                     {
 #pragma unroll
@@ -1057,7 +1114,11 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
                     uint32_t pk[32];
 #pragma unroll
                     for (int i = 0; i < 32; i++)
-                        pk[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+                    {
+                        float a0, a1;
+                        mul_x2(a0, a1, __uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]), inv);
+                        pk[i] = pack_bf16x2(a0, a1);
+                    }
                     if (a.out_v8)
                     {
 #pragma unroll
