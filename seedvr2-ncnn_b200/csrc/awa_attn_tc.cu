@@ -282,6 +282,10 @@ __device__ __forceinline__ uint64_t block_mask(const AttnArgs& a, const Job& job
     const int w_a = max(woff, 0), w_b = min(woff + job.win.nw, a.plan.tc_bwc);
     if (h_a >= h_b || w_a >= w_b)
         return 0ull;
+    // a box inside its window (every box of an unclipped window) covers all
+    // 64 rows: skip the row loop, which every softmax and RoPE thread runs per block
+    if (h_a == 0 && w_a == 0 && h_b == a.plan.tc_bhc && w_b == a.plan.tc_bwc && h_b * w_b == kKeys)
+        return ~0ull;
     const uint64_t row = low_bits(w_b) & ~low_bits(w_a);
     uint64_t m = 0ull;
     for (int h = h_a; h < h_b; h++)
