@@ -118,6 +118,7 @@ struct Job
     int vblocks;  // fused: video blocks (the rest are text blocks)
     int length;   // window rows (video + text)
     bool has_b;   // second query tile exists
+    bool full;    // fused: every video box lies inside the window (all 64 rows are window rows)
 };
 
 // The global-memory part of a job (its work item and window).
@@ -191,6 +192,9 @@ __device__ __forceinline__ Job decode_job(const AttnArgs& a, int j, const JobSou
     }
     job.qa = 2 * item.y;
     job.has_b = 2 * (job.qa + 1) < job.blocks;
+    job.full = !PACKED && job.win.h0 == job.win.h0n && job.win.w0 == job.win.w0n &&
+               job.win.nh >= a.plan.tc_nhc * a.plan.tc_bhc && job.win.nw >= a.plan.tc_nwc * a.plan.tc_bwc &&
+               a.plan.tc_bhc * a.plan.tc_bwc == kKeys;
     return job;
 }
 
@@ -275,6 +279,8 @@ __device__ __forceinline__ uint64_t block_mask(const AttnArgs& a, const Job& job
         return low_bits(job.length - g.first);
     if (!g.video)
         return low_bits(a.plan.text_tokens - g.first);
+    if (job.full)
+        return ~0ull;
     // window part of the box: rows [h_a, h_b) x columns [w_a, w_b) of the box
     const int hoff = job.win.h0 - job.win.h0n - g.hb;
     const int woff = job.win.w0 - job.win.w0n - g.wb;
@@ -365,11 +371,10 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
 // One panel (64 features) of block b's rows of segment m (0 q, 1 k, 2 v)
 // into shared memory at dst.
 template <bool PACKED>
-__device__ __forceinline__ void load_block_panel(const AttnArgs& a, const TmaMaps& maps, const Job& job, int b,
-                                                 int m, int panel, uint32_t dst, uint64_t* bar)
+__device__ __forceinline__ void load_block_panel(const AttnArgs& a, const TmaMaps& maps, const Job& job,
+                                                 const BlockGeo& g, int m, int panel, uint32_t dst, uint64_t* bar)
 {
     const int x = job.head * kHeadDim + 64 * panel;
-    const BlockGeo g = block_geo<PACKED>(a, job, b);
     if (PACKED)
         tma_load_2d(dst, &maps.map[0][m], x, job.win.offset + g.first, bar);
     else if (g.video)
@@ -609,11 +614,13 @@ __device__ void tma_role(const AttnArgs& a, const TmaMaps& maps, TcShared& sh, i
         {
             const int qb = lane >> 1, panel = lane & 1;  // block qb0 + qb -> tile qb/2, rows 64*(qb%2)
             const uint32_t dst = tc::smem_addr(sh.q[qb >> 1]) + (uint32_t)(panel * kQPanel + (qb & 1) * kKeys * 128);
-            load_block_panel<PACKED>(a, maps, job, qb0 + qb, 0, panel, dst, &sh.bar.q_loaded);
+            load_block_panel<PACKED>(a, maps, job, block_geo<PACKED>(a, job, qb0 + qb), 0, panel, dst,
+                                     &sh.bar.q_loaded);
         }
         q_issued++;
         // ---- K/V blocks through the ring: lanes 0-3 = (K, V) x panel
-        for (int kb = 0; kb < job.blocks; kb++)
+        BlockCursor cur;  // the blocks' geometry without divisions
+        for (int kb = 0; kb < job.blocks; kb++, cur.next(a))
         {
             const int stage = g % kStages;
             const uint32_t use = g / kStages;
@@ -629,7 +636,8 @@ __device__ void tma_role(const AttnArgs& a, const TmaMaps& maps, TcShared& sh, i
             {
                 const int kv = lane >> 1, panel = lane & 1;
                 const uint32_t dst = tc::smem_addr(sh.kv[stage][kv]) + (uint32_t)(panel * kKvPanel);
-                load_block_panel<PACKED>(a, maps, job, kb, 1 + kv, panel, dst, &sh.bar.kv_loaded[stage]);
+                load_block_panel<PACKED>(a, maps, job, cur.geo<PACKED>(a, job), 1 + kv, panel, dst,
+                                         &sh.bar.kv_loaded[stage]);
             }
             g++;
         }
