@@ -168,6 +168,21 @@ __device__ __forceinline__ void store4(T* dst, int col, int hd, float a0, float 
             store1(dst + col + j, vals[j]);
 }
 
+// d += a * (b0, b1) on a register pair: sm_100 issues two fp32 FMAs per
+// instruction (.f32x2); each lane rounds exactly as fmaf does, so the sums
+// are the scalar loop's, bit for bit.
+__device__ __forceinline__ void fma_bcast_x2(float& d0, float& d1, float a, float b0, float b1)
+{
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %2};\n\t"
+        "mov.b64 rb, {%3, %4};\n\t"
+        "mov.b64 rd, {%0, %1};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rd;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "+f"(d0), "+f"(d1)
+        : "f"(a), "f"(b0), "f"(b1));
+}
+
 template <bool PACKED, bool VEC, typename TIn, typename TOut>
 __global__ void __launch_bounds__(kThreads, 2) attention_simt_kernel(const AttnArgs a)
 {
@@ -247,8 +262,8 @@ __global__ void __launch_bounds__(kThreads, 2) attention_simt_kernel(const AttnA
 #pragma unroll
             for (int i = 0; i < 4; i++)
 #pragma unroll
-                for (int j = 0; j < 4; j++)
-                    s[i][j] = fmaf(qv[i], kv[j], s[i][j]);
+                for (int j = 0; j < 4; j += 2)
+                    fma_bcast_x2(s[i][j], s[i][j + 1], qv[i], kv[j], kv[j + 1]);
         }
 
         // Online softmax over this key block (rows shared by the 16 lanes of a half-warp).
@@ -306,8 +321,8 @@ __global__ void __launch_bounds__(kThreads, 2) attention_simt_kernel(const AttnA
                 {
                     const float pv = u == 0 ? p4[i].x : u == 1 ? p4[i].y : u == 2 ? p4[i].z : p4[i].w;
 #pragma unroll
-                    for (int j = 0; j < 8; j++)
-                        acc[i][j] = fmaf(pv, vv[j], acc[i][j]);
+                    for (int j = 0; j < 8; j += 2)
+                        fma_bcast_x2(acc[i][j], acc[i][j + 1], pv, vv[j], vv[j + 1]);
                 }
             }
         }
