@@ -521,6 +521,94 @@ def run_qkv_proj(args, rank, world, local_rank):
     }
 
 
+def run_layers(args, rank, world, local_rank):
+    """--stage layers: the reference's four-layer chain as separate passes
+    (Pack -> MMRoPE -> WindowAttention -> Unpack, the path an ncnn graph with the
+    four layer classes takes) on the workload, each kernel timed by the
+    library's launch profiler and set against the HBM peak with its algorithmic
+    bytes: the gather (Pack), the rotation (MMRoPE), the packed attention, the
+    video scatter and the text mean. A step is one pass of the chain; inputs
+    resident in HBM."""
+    import torch
+    import torch.distributed as dist
+
+    import awa_b200
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    grid, num, shifted, precision, _ = WORKLOADS[args.workload]
+    bf16 = precision == "bf16"
+    dtype = torch.bfloat16 if bf16 else torch.float32
+    esize = 2 if bf16 else 4
+    prec = awa_b200.AWA_PREC_BF16 if bf16 else awa_b200.AWA_PREC_FP32
+    n_v = grid[0] * grid[1] * grid[2]
+    plan = awa_b200.AwaPlan(*grid, *num, TEXT, bool(shifted))
+    info = plan.info
+    gen = torch.Generator(device=device).manual_seed(777 + rank)
+    video = torch.randn(n_v, 3, HEADS, HEAD_DIM, device=device, generator=gen).to(dtype)
+    text = torch.randn(TEXT, 3, HEADS, HEAD_DIM, device=device, generator=gen).to(dtype)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        packed, _ = plan.pack(video, text, stream=stream)
+        roped = plan.mmrope(packed, stream=stream)
+        attended = plan.window_attention(roped, prec, stream=stream)
+        return plan.unpack(attended, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    awa_b200.device_status()
+    awa_b200.profile_reset()
+    awa_b200.profile_enable(True)
+    clocks = ClockSampler(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                          int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank]))
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    stop.record(stream)
+    torch.cuda.synchronize()
+    clock = clocks.stop()
+    awa_b200.profile_enable(False)
+    prof = awa_b200.profile_collect()
+    awa_b200.device_status()
+    ms_per_step = start.elapsed_time(stop) / args.steps
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            hbm_peak, peak_src = float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, ValueError, KeyError):
+        hbm_peak, peak_src = 6650.0, "fallback"
+    s_rows, w, row = info.sequence_tokens, info.window_count, HEADS * HEAD_DIM
+    attn_name = "awa_attention_tc_packed" if bf16 else "awa_attention_simt_packed"
+    # algorithmic bytes per launch: each source row read once, each output row written once
+    alg = {
+        "awa_pack": (n_v + TEXT) * 3 * row * esize + s_rows * 3 * row * esize + (w + 1) * 4,
+        "awa_mmrope": 2 * s_rows * 3 * row * esize,
+        attn_name: s_rows * 3 * row * esize + s_rows * row * esize,
+        "awa_unpack_video": 2 * n_v * row * esize,
+        "awa_text_reduce": w * TEXT * row * esize + TEXT * row * esize,
+    }
+    kernels = {}
+    for name, nbytes in alg.items():
+        launches, total = prof.get(name, (0, 0.0))
+        if not launches:
+            continue
+        kms = total / launches
+        gbs = nbytes / (kms / 1000.0) / 1e9
+        kernels[name] = {"ms": round(kms, 5), "bytes": nbytes, "gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4)}
+    return {
+        "metric": "AWA layer chain as separate passes (Pack, MMRoPE, WindowAttention, Unpack) windows/s per B200",
+        "value": round(info.window_count * world / (ms_per_step / 1000.0), 2), "unit": "windows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if bf16 else "f32", "data": "synthetic N(0,1) QKV",
+        "config": {"workload": f"{args.workload}-layers", "grid": list(grid), "num_windows": list(num),
+                   "shifted": bool(shifted), "windows": info.window_count, "sequence_rows": s_rows},
+        "gpu_launches": sum(v[0] for v in prof.values()),
+        "kernels": kernels, "hbm_peak_gbs": hbm_peak, "peak_source": peak_src, "clocks": clock,
+    }
+
+
 STACK_BLOCKS, STACK_FP32_BLOCKS = 32, 9
 
 
@@ -673,9 +761,10 @@ def main():
     parser.add_argument("--e2e-steps", type=int, default=20)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiler captures)")
-    parser.add_argument("--stage", default="awa", choices=["awa", "qkv-proj", "out-proj", "stack"],
+    parser.add_argument("--stage", default="awa", choices=["awa", "qkv-proj", "out-proj", "stack", "layers"],
                         help="awa: the AWA layer (the headline); qkv-proj / out-proj: its input's producer / "
-                             "its output's consumer; stack: the attention path of 32 blocks via the stack driver")
+                             "its output's consumer; stack: the attention path of 32 blocks via the stack driver; layers: "
+                             "the four layers as separate passes, per-kernel HBM throughput")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
@@ -699,8 +788,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.stage in ("qkv-proj", "out-proj", "stack"):
-            line = (run_stack if args.stage == "stack" else run_qkv_proj)(args, rank, world, local_rank)
+        if args.stage in ("qkv-proj", "out-proj", "stack", "layers"):
+            runner = {"stack": run_stack, "layers": run_layers}.get(args.stage, run_qkv_proj)
+            line = runner(args, rank, world, local_rank)
             if rank == 0:
                 print(json.dumps(line), flush=True)
             return

@@ -65,8 +65,9 @@ __global__ void pack_chunks(PlanDevice plan, int head_row, const TIn* __restrict
     const int64_t step = (int64_t)gridDim.x * blockDim.x;
     for (int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; id < total; id += step)
     {
-        const int position = (int)(id / chunks_per_row);
-        const int c = (int)(id - (int64_t)position * chunks_per_row);
+        const unsigned uid = (unsigned)id;  // 32-bit: the launch checks total < 2^32
+        const int position = (int)(uid / (unsigned)chunks_per_row);
+        const int c = (int)(uid - (unsigned)position * (unsigned)chunks_per_row);
         const int qkv = c / chunks_per_qkv;
         const int e = (c - qkv * chunks_per_qkv) * 8;
         const int source = __ldg(plan.sequence_index + position);
@@ -119,7 +120,8 @@ __device__ __forceinline__ void rotate_pair(float x0, float x1, float c, float s
 
 __device__ __forceinline__ float2 rope_cs(const PlanDevice& plan, short4 coords, int pair)
 {
-    const int axis = pair / plan.pairs_per_axis;
+    // pair < rope_dim / 2 = 3 pairs_per_axis: the axis by two compares, not a division
+    const int axis = (pair >= plan.pairs_per_axis) + (pair >= 2 * plan.pairs_per_axis);
     const int within = pair - axis * plan.pairs_per_axis;
     const int coord = axis == 0 ? coords.x : axis == 1 ? coords.y : coords.z;
     return __ldg(plan.rope_table + coord * plan.pairs_per_axis + within);
@@ -135,8 +137,9 @@ __global__ void mmrope_chunks(PlanDevice plan, int heads, int head_dim, const TI
     const short4* coords_table = reinterpret_cast<const short4*>(plan.position_coords);
     for (int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; id < total; id += step)
     {
-        const int position = (int)(id / chunks_per_row);
-        const int e = (int)(id - (int64_t)position * chunks_per_row) * 8;
+        const unsigned uid = (unsigned)id;  // 32-bit: the launch checks total < 2^32
+        const int position = (int)(uid / (unsigned)chunks_per_row);
+        const int e = (int)(uid - (unsigned)position * (unsigned)chunks_per_row) * 8;
         const int qkv_head = e / head_dim;
         const int f = e - qkv_head * head_dim;
         float v[8];
@@ -415,7 +418,7 @@ struct PackLaunch
         const bool vec = chunkable(head_row, sizeof(TIn), ptrs, 2, in_strides, 4) &&
                          chunkable(head_row, sizeof(TOut), ptrs + 2, 1, &pts, 1);
         const int threads = 256;
-        if (vec)
+        if (vec && (int64_t)plan.sequence_tokens * 3 * head_row / 8 < (int64_t)1 << 32)
             pack_chunks<TIn, TOut><<<grid_for((int64_t)plan.sequence_tokens * 3 * head_row / 8, threads), threads, 0,
                                      stream>>>(plan, head_row, (const TIn*)video, vts, vqs, (const TIn*)text, tts, tqs,
                                                (TOut*)packed, pts, cu_out);
@@ -438,7 +441,7 @@ struct MmropeLaunch
         const bool vec = head_dim % 8 == 0 && chunkable(3 * heads * head_dim, sizeof(TIn), pin, 1, &its, 1) &&
                          chunkable(3 * heads * head_dim, sizeof(TOut), pout, 1, &ots, 1);
         const int threads = 256;
-        if (vec)
+        if (vec && (int64_t)plan.sequence_tokens * 3 * heads * head_dim / 8 < (int64_t)1 << 32)
             mmrope_chunks<TIn, TOut><<<grid_for((int64_t)plan.sequence_tokens * 3 * heads * head_dim / 8, threads),
                                        threads, 0, stream>>>(plan, heads, head_dim, (const TIn*)in, its, (TOut*)out, ots);
         else
