@@ -135,12 +135,14 @@ __global__ void mmrope_chunks(PlanDevice plan, int heads, int head_dim, const TI
     const int64_t total = (int64_t)plan.sequence_tokens * chunks_per_row;
     const int64_t step = (int64_t)gridDim.x * blockDim.x;
     const short4* coords_table = reinterpret_cast<const short4*>(plan.position_coords);
+    // e / head_dim by a multiply-high: exact while e * head_dim < 2^32 (the launch checks it)
+    const uint32_t hd_magic = (uint32_t)((((uint64_t)1 << 32) + head_dim - 1) / head_dim);
     for (int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; id < total; id += step)
     {
         const unsigned uid = (unsigned)id;  // 32-bit: the launch checks total < 2^32
         const int position = (int)(uid / (unsigned)chunks_per_row);
         const int e = (int)(uid - (unsigned)position * (unsigned)chunks_per_row) * 8;
-        const int qkv_head = e / head_dim;
+        const int qkv_head = (int)__umulhi((uint32_t)e, hd_magic);
         const int f = e - qkv_head * head_dim;
         float v[8];
         load8(in + (int64_t)position * its + e, v);
@@ -441,7 +443,8 @@ struct MmropeLaunch
         const bool vec = head_dim % 8 == 0 && chunkable(3 * heads * head_dim, sizeof(TIn), pin, 1, &its, 1) &&
                          chunkable(3 * heads * head_dim, sizeof(TOut), pout, 1, &ots, 1);
         const int threads = 256;
-        if (vec && (int64_t)plan.sequence_tokens * 3 * heads * head_dim / 8 < (int64_t)1 << 32)
+        if (vec && (int64_t)plan.sequence_tokens * 3 * heads * head_dim / 8 < (int64_t)1 << 32 &&
+            (int64_t)3 * heads * head_dim * head_dim < (int64_t)1 << 32)
             mmrope_chunks<TIn, TOut><<<grid_for((int64_t)plan.sequence_tokens * 3 * heads * head_dim / 8, threads),
                                        threads, 0, stream>>>(plan, heads, head_dim, (const TIn*)in, its, (TOut*)out, ots);
         else
