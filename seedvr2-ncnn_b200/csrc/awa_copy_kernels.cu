@@ -476,6 +476,52 @@ struct UnpackVideoLaunch
     }
 };
 
+// text_reduce for the Unpack layer's packed rows, two consecutive elements
+// per thread: window w's text row i is packed row cu_seqlens[w + 1] - text +
+// i; each term is divided by the window count before it is added, in window
+// order, as the reference's Unpack does (bit-exact with text_reduce).
+template <typename TIn, typename TOut>
+__global__ void text_reduce_packed_v2(PlanDevice plan, int head_row, const TIn* __restrict__ src, int64_t sts,
+                                      int window_begin, int window_end, float divisor, TOut* __restrict__ out,
+                                      int64_t ots)
+{
+    const int text = plan.text_tokens;
+    const int pairs = head_row >> 1;
+    const int total = text * pairs;
+    for (int id = blockIdx.x * blockDim.x + threadIdx.x; id < total; id += gridDim.x * blockDim.x)
+    {
+        const int i = id / pairs;
+        const int e = (id - i * pairs) * 2;
+        const TIn* col = src + (int64_t)(i - text) * sts + e;  // + cu_seqlens[w + 1] * sts
+        constexpr int kBatch = sizeof(TIn) == 2 ? 32 : 16;
+        float2 acc = make_float2(0.f, 0.f);
+        int w = window_begin;
+        for (; w + kBatch <= window_end; w += kBatch)
+        {
+            decltype(raw_pair_cs(col)) x[kBatch];
+#pragma unroll
+            for (int u = 0; u < kBatch; u++)
+                x[u] = raw_pair_cs(col + (int64_t)__ldg(plan.cu_seqlens + w + u + 1) * sts);
+#pragma unroll
+            for (int u = 0; u < kBatch; u++)
+            {
+                const float2 v = widen_pair(x[u]);
+                acc.x = __fadd_rn(acc.x, __fdiv_rn(v.x, divisor));
+                acc.y = __fadd_rn(acc.y, __fdiv_rn(v.y, divisor));
+            }
+        }
+        for (; w < window_end; w++)
+        {
+            const float2 v = load_pair_cs(col + (int64_t)__ldg(plan.cu_seqlens + w + 1) * sts);
+            acc.x = __fadd_rn(acc.x, __fdiv_rn(v.x, divisor));
+            acc.y = __fadd_rn(acc.y, __fdiv_rn(v.y, divisor));
+        }
+        TOut* o = out + (int64_t)i * ots + e;
+        store1(o, acc.x);
+        store1(o + 1, acc.y);
+    }
+}
+
 template <typename TIn, typename TOut>
 struct TextReduceLaunch
 {
@@ -490,6 +536,14 @@ struct TextReduceLaunch
             text_reduce_v2<TIn, TOut><<<grid_for(pairs, threads), threads, 0, stream>>>(
                 plan.text_tokens, head_row, (const TIn*)src, sts, window_end - window_begin, divisor, (TOut*)out,
                 ots);
+            return (int)cudaGetLastError();
+        }
+        if (packed && divisor != 0.f && head_row % 2 == 0 && sts % 2 == 0 &&
+            reinterpret_cast<uintptr_t>(src) % (2 * sizeof(TIn)) == 0 && (int64_t)plan.text_tokens * head_row < (1 << 30))
+        {
+            const int64_t pairs = (int64_t)plan.text_tokens * (head_row / 2);
+            text_reduce_packed_v2<TIn, TOut><<<grid_for(pairs, threads), threads, 0, stream>>>(
+                plan, head_row, (const TIn*)src, sts, window_begin, window_end, divisor, (TOut*)out, ots);
             return (int)cudaGetLastError();
         }
         text_reduce<TIn, TOut><<<grid_for((int64_t)plan.text_tokens * head_row, threads), threads, 0, stream>>>(
