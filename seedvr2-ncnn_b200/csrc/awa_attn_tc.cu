@@ -392,22 +392,6 @@ __device__ __forceinline__ void st_global_v8(void* p, uint32_t r0, uint32_t r1, 
                  : "memory");
 }
 
-// Barrier over the 128 RoPE threads that also ANDs their flags, so a wait
-// that gave up in one thread makes every RoPE thread leave together.
-__device__ __forceinline__ bool rope_all(bool ok)
-{
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.and.pred q, 1, 128, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)ok)
-        : "memory");
-    return r != 0;
-}
-
 // Warp-uniform outcome of a bounded wait (tcgen05.ld/st are warp-collective).
 __device__ __forceinline__ bool warp_all(bool ok)
 {
@@ -685,10 +669,10 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
         const Job job = decode_job<PACKED>(a, j, pre.advance(a, j, njobs));
         const int hoff = job.win.h0 - job.win.h0n, woff = job.win.w0 - job.win.w0n;
         // ---- Q: staging -> (rotate) -> TMEM
-        if (!rope_all(wait_bar(&sh.bar.q_loaded, q_loaded_phase, abort, a.error_flag, 11)))
+        if (!warp_all(wait_bar(&sh.bar.q_loaded, q_loaded_phase, abort, a.error_flag, 11)))
             return;
         q_loaded_phase ^= 1;
-        if (!rope_all(wait_bar(&sh.bar.q_empty, q_empty_phase, abort, a.error_flag, 12)))
+        if (!warp_all(wait_bar(&sh.bar.q_empty, q_empty_phase, abort, a.error_flag, 12)))
             return;
         q_empty_phase ^= 1;
         tc::fence_after_sync();
@@ -730,7 +714,7 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
             const uint32_t use = g / kStages;
             const BlockGeo geo = cur.geo<PACKED>(a, job);
             const uint64_t mask = block_mask<PACKED>(a, job, geo);
-            if (!rope_all(wait_bar(&sh.bar.kv_loaded[stage], use & 1, abort, a.error_flag, 13)))
+            if (!warp_all(wait_bar(&sh.bar.kv_loaded[stage], use & 1, abort, a.error_flag, 13)))
                 return;
             if (!PACKED)
             {
