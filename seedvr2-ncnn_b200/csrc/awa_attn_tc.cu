@@ -663,15 +663,55 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
     // block, and its K row)
     const int row_h = (ptid & 63) / bwc, row_w = (ptid & 63) % bwc;
 
+    // The job's Q tiles, rotated in place in the staging area once loaded. It
+    // runs for the next job right after this job's K blocks, while the MMA warp
+    // still works on this job, so that at the job boundary Q only has to be
+    // copied into TMEM.
+    auto prepare_q = [&](const Job& job) -> bool {
+        if (!warp_all(wait_bar(&sh.bar.q_loaded, q_loaded_phase, abort, a.error_flag, 11)))
+            return false;
+        q_loaded_phase ^= 1;
+        if (PACKED)
+            return true;
+        const int hoff = job.win.h0 - job.win.h0n, woff = job.win.w0 - job.win.w0n;
+#pragma unroll 1
+        for (int t = 0; t < 2; t++)
+        {
+            if (t == 1 && !job.has_b)
+                break;
+            uint8_t* tile = sh.q[t];
+            int base[3];
+            const int b = 2 * (job.qa + t) + (ptid >> 6);
+            const BlockGeo geo = block_geo<PACKED>(a, job, b);
+            const bool valid = b < job.blocks && ((block_mask<PACKED>(a, job, geo) >> (ptid & 63)) & 1ull);
+            row_bases(base, valid, geo, a.plan.text_tokens, row_h, row_w, hoff, woff, ptid & 63, ppa);
+            uint32_t words[32];
+            load_half_row(words, tile, kQRows, ptid, 0);
+            rotate_half_row<0, RD>(words, base, table, ppa, rope_dim);
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                *reinterpret_cast<uint4*>(tile + swizzled_offset(kQRows, ptid, k)) =
+                    make_uint4(words[4 * k], words[4 * k + 1], words[4 * k + 2], words[4 * k + 3]);
+            load_half_row(words, tile, kQRows, ptid, 1);
+            rotate_half_row<1, RD>(words, base, table, ppa, rope_dim);
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                *reinterpret_cast<uint4*>(tile + swizzled_offset(kQRows, ptid, 8 + k)) =
+                    make_uint4(words[4 * k], words[4 * k + 1], words[4 * k + 2], words[4 * k + 3]);
+        }
+        return true;
+    };
+
     JobPrefetch pre(a, njobs);
+    bool prepared = false;  // this job's Q already rotated in the staging area
     for (int j = blockIdx.x; j < njobs; j += gridDim.x)
     {
         const Job job = decode_job<PACKED>(a, j, pre.advance(a, j, njobs));
         const int hoff = job.win.h0 - job.win.h0n, woff = job.win.w0 - job.win.w0n;
-        // ---- Q: staging -> (rotate) -> TMEM
-        if (!warp_all(wait_bar(&sh.bar.q_loaded, q_loaded_phase, abort, a.error_flag, 11)))
+        if (!prepared && !prepare_q(job))
             return;
-        q_loaded_phase ^= 1;
+        prepared = false;
+        // ---- Q: staging (rotated) -> TMEM
         if (!warp_all(wait_bar(&sh.bar.q_empty, q_empty_phase, abort, a.error_flag, 12)))
             return;
         q_empty_phase ^= 1;
@@ -682,22 +722,10 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
             if (t == 1 && !job.has_b)
                 break;
             const uint8_t* tile = sh.q[t];
-            int base[3] = {0, 0, 0};
-            if (!PACKED)
-            {
-                const int b = 2 * (job.qa + t) + (ptid >> 6);
-                const BlockGeo geo = block_geo<PACKED>(a, job, b);
-                const bool valid = b < job.blocks && ((block_mask<PACKED>(a, job, geo) >> (ptid & 63)) & 1ull);
-                row_bases(base, valid, geo, a.plan.text_tokens, row_h, row_w, hoff, woff, ptid & 63, ppa);
-            }
             uint32_t words[32];
             load_half_row(words, tile, kQRows, ptid, 0);
-            if (!PACKED)
-                rotate_half_row<0, RD>(words, base, table, ppa, rope_dim);
             tc::tmem_st32(tmem + lane_base + kColQ + 64u * t, words);
             load_half_row(words, tile, kQRows, ptid, 1);
-            if (!PACKED)
-                rotate_half_row<1, RD>(words, base, table, ppa, rope_dim);
             tc::tmem_st32(tmem + lane_base + kColQ + 64u * t + 32u, words);
         }
         tc::tmem_wait_st();
@@ -748,6 +776,12 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
                 tc::fence_async_smem();
             }
             mbar_arrive(&sh.bar.kv_full[stage]);
+        }
+        if (j + (int)gridDim.x < njobs)
+        {
+            if (!prepare_q(decode_job<PACKED>(a, j + gridDim.x, pre.next)))
+                return;
+            prepared = true;
         }
     }
 }
