@@ -711,22 +711,26 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
         if (!prepared && !prepare_q(job))
             return;
         prepared = false;
-        // ---- Q: staging (rotated) -> TMEM
-        if (!warp_all(wait_bar(&sh.bar.q_empty, q_empty_phase, abort, a.error_flag, 12)))
-            return;
-        q_empty_phase ^= 1;
-        tc::fence_after_sync();
-#pragma unroll 1
-        for (int t = 0; t < 2; t++)
+        // ---- Q: staging (rotated) -> TMEM; tile A's row is read before the
+        // wait for the TMEM columns, so that only the stores follow it
         {
-            if (t == 1 && !job.has_b)
-                break;
-            const uint8_t* tile = sh.q[t];
+            uint32_t a0[32], a1[32];
+            load_half_row(a0, sh.q[0], kQRows, ptid, 0);
+            load_half_row(a1, sh.q[0], kQRows, ptid, 1);
+            if (!warp_all(wait_bar(&sh.bar.q_empty, q_empty_phase, abort, a.error_flag, 12)))
+                return;
+            q_empty_phase ^= 1;
+            tc::fence_after_sync();
+            tc::tmem_st32(tmem + lane_base + kColQ, a0);
+            tc::tmem_st32(tmem + lane_base + kColQ + 32u, a1);
+        }
+        if (job.has_b)
+        {
             uint32_t words[32];
-            load_half_row(words, tile, kQRows, ptid, 0);
-            tc::tmem_st32(tmem + lane_base + kColQ + 64u * t, words);
-            load_half_row(words, tile, kQRows, ptid, 1);
-            tc::tmem_st32(tmem + lane_base + kColQ + 64u * t + 32u, words);
+            load_half_row(words, sh.q[1], kQRows, ptid, 0);
+            tc::tmem_st32(tmem + lane_base + kColQ + 64u, words);
+            load_half_row(words, sh.q[1], kQRows, ptid, 1);
+            tc::tmem_st32(tmem + lane_base + kColQ + 96u, words);
         }
         tc::tmem_wait_st();
         tc::fence_before_sync();
