@@ -58,6 +58,8 @@ WORKLOADS = {
 
 
 def window_costs(grid, num, shifted):
+    """Windows and their lengths (video tokens + text) from the library's plan
+    rule (the B200 arm)."""
     import awa_b200
 
     wins = awa_b200.make_windows(grid, num, bool(shifted))
@@ -65,29 +67,71 @@ def window_costs(grid, num, shifted):
     return wins, lengths
 
 
+def reference_windows(grid, num, shifted):
+    """The same windows from the reference's own make_awa_windows (oracle/_ref),
+    so the reference arm loads nothing of the B200 library."""
+    from oracle.oracle import Reference
+
+    return Reference().make_windows(grid, num, bool(shifted))
+
+
 def attention_flops(lengths, heads=HEADS, head_dim=HEAD_DIM):
     return float(sum(4.0 * L * L * head_dim * heads for L in lengths))
 
 
+def workload_config(name, world, mode="replicas"):
+    """The `config` both arms print for a workload (identical keys and values)."""
+    grid, num, shifted, precision, desc = WORKLOADS[name]
+    n_v = grid[0] * grid[1] * grid[2]
+    esize = 2 if precision == "bf16" else 4
+    in_bytes = (n_v + TEXT) * 3 * HEADS * HEAD_DIM * esize
+    parallelism = (f"sharded: one layer's windows split over {world} GPU(s), NCCL text all-reduce + video all-gather"
+                   if mode == "sharded" else f"replicas: {world} independent layer(s), one per GPU")
+    return {"workload": name, "description": desc, "grid": list(grid), "num_windows": list(num),
+            "shifted": bool(shifted), "heads": HEADS, "head_dim": HEAD_DIM, "text_tokens": TEXT, "rope_dim": 126,
+            "precision": precision, "l2": f"inputs {in_bytes / 1e9:.2f} GB per step > 126 MB L2; no flush",
+            "parallelism": parallelism}
+
+
 # ----------------------------------------------------------------------------- CPU baseline
-def _ref_sample_worker(args):
-    """Runs the reference's CPU chain on one sample; returns (seconds, sum L^2 * heads)."""
-    grid, num, heads, seed = args
+_REF = None
+_REF_INPUTS = {}
+
+
+def _ref_window_worker(args):
+    """The reference's CPU chain (Pack -> MMRoPE -> WindowAttention -> Unpack,
+    awa_layers.cpp:419-458, 913-953, 1062-1120, 638-689, compiled unmodified in
+    oracle/_ref) on windows of the workload, one at a time. A grid of a window's
+    size with num_windows (1,1,1) holds exactly that window: the same video
+    tokens, the 58 text tokens, the same window-local RoPE coordinates and the
+    same attention. Returns (seconds inside the reference forward, windows)."""
+    global _REF
+    dims_list, heads = args
     import numpy as np
 
     from oracle.oracle import LayerConfig, Reference
 
-    ref = Reference()
-    cfg = LayerConfig(*grid, *num, text_tokens=TEXT, shifted=0, heads=heads, head_dim=HEAD_DIM)
-    rng = np.random.default_rng(seed)
-    v = rng.standard_normal((cfg.source_tokens, 3, heads, HEAD_DIM), dtype=np.float32)
-    t = rng.standard_normal((TEXT, 3, heads, HEAD_DIM), dtype=np.float32)
-    start = time.perf_counter()
-    ref.chain(cfg, v, t)
-    seconds = time.perf_counter() - start
-    wins = ref.make_windows(grid, num, False)
-    work = sum(((w[1] - w[0]) * (w[3] - w[2]) * (w[5] - w[4]) + TEXT) ** 2 for w in wins) * heads
-    return seconds, work
+    if _REF is None:
+        _REF = Reference()
+    seconds = 0.0
+    for dims in dims_list:
+        cfg = LayerConfig(*dims, 1, 1, 1, text_tokens=TEXT, shifted=0, heads=heads, head_dim=HEAD_DIM)
+        key = (tuple(dims), heads)
+        if key not in _REF_INPUTS:
+            wins = _REF.make_windows(dims, (1, 1, 1), False)
+            assert wins == [(0, dims[0], 0, dims[1], 0, dims[2])], (dims, wins)
+            rng = np.random.default_rng(sum(dims) * 131 + heads)
+            _REF_INPUTS[key] = (rng.standard_normal((cfg.source_tokens, 3, heads, HEAD_DIM), dtype=np.float32),
+                                rng.standard_normal((TEXT, 3, heads, HEAD_DIM), dtype=np.float32))
+        v, t = _REF_INPUTS[key]
+        start = time.perf_counter()
+        _REF.chain(cfg, v, t)
+        seconds += time.perf_counter() - start
+    return seconds, len(dims_list)
+
+
+def _window_dims(windows):
+    return [(w[1] - w[0], w[3] - w[2], w[5] - w[4]) for w in windows]
 
 
 def cpu_kind():
@@ -96,72 +140,79 @@ def cpu_kind():
     return "reference" if Reference.available() else "port"
 
 
-def cpu_baseline_single(workload_work, workload_windows, budget_s=12.0):
-    """Reference CPU forward, 1 core, on 4 windows of the cfg4 window shape
-    (grid 4x16x16, num_windows 1,8,8: four 4x8x8 windows + 58 text tokens,
-    20 heads), repeated for ~budget_s; scaled to the workload by sum(L^2)."""
-    sample = ((4, 16, 16), (1, 8, 8), HEADS)
-    total_s, total_work, reps = 0.0, 0.0, 0
-    while total_s < budget_s and reps < 8:
-        s, w = _ref_sample_worker((*sample, reps))
+def cpu_baseline_single(name, budget_s=12.0):
+    """The reference CPU forward on 1 core, for ~budget_s, on the workload's own
+    windows in plan order (a contiguous run of the window list, which cycles
+    through every window shape of the layer); value = windows / seconds."""
+    grid, num, shifted, _, _ = WORKLOADS[name]
+    dims = _window_dims(reference_windows(grid, num, shifted))
+    total_s, done = 0.0, 0
+    while total_s < budget_s and done < len(dims):
+        s, n = _ref_window_worker(([dims[done]], HEADS))
         total_s += s
-        total_work += w
-        reps += 1
-    layer_seconds = total_s * (workload_work / total_work)
+        done += n
     return {
-        "value": workload_windows / layer_seconds,
+        "value": done / total_s,
         "unit": UNIT,
         "cores": 1,
         "kind": cpu_kind(),
-        "sample": f"{reps} runs of the reference Pack->MMRoPE->WindowAttention->Unpack CPU forward on a "
-                  f"4x16x16 grid with num_windows (1,8,8): 4 windows of 4x8x8 video + {TEXT} text tokens, "
-                  f"{HEADS} heads x {HEAD_DIM} (cfg4's window shape), {total_s:.1f} s; scaled to the workload "
-                  f"by sum(L^2)*heads",
+        "sample": f"windows 0..{done - 1} of the workload's {len(dims)} (plan order, every window shape), each "
+                  f"through the reference's Pack->MMRoPE->WindowAttention->Unpack CPU forward with {HEADS} heads x "
+                  f"{HEAD_DIM} and {TEXT} text tokens, {total_s:.1f} s on 1 core",
         "seconds": round(total_s, 3),
     }
 
 
 def run_reference_arm(args, rank, world):
-    """--impl reference: the reference CPU path on every host core (rank 0 only)."""
+    """--impl reference: the reference's own CPU forward of the AWA chain on
+    every host core (one process per core; the reference code is
+    single-threaded), rank 0 only. A step runs a fixed deterministic sample of
+    the workload's own windows, split over the processes: the whole layer
+    (every window once) when that fits the time budget, else the next run of
+    the window list in rotation, so that over the timed steps every window
+    shape appears in its share. value = windows processed / elapsed."""
     if rank != 0:
         return None
     name = args.workload
     grid, num, shifted, precision, desc = WORKLOADS[name]
-    _, lengths = window_costs(grid, num, shifted)
-    workload_work = sum(L * L for L in lengths) * HEADS
+    dims = _window_dims(reference_windows(grid, num, shifted))
+    W = len(dims)
     cores = os.cpu_count() or 1
-    # One cfg4-shaped window per worker per step; heads trimmed so the whole
-    # run stays within ~4 minutes.
-    per_window_s = 0.55
-    heads = HEADS
-    budget = 240.0
-    if (args.steps + args.warmup) * per_window_s > budget:
-        heads = max(1, int(HEADS * budget / ((args.steps + args.warmup) * per_window_s)))
-    sample = ((4, 8, 8), (1, 8, 8), heads)
     ctx = mp.get_context("spawn")
     with ctx.Pool(cores) as pool:
+        # warm-up: every process loads the reference and runs one window
+        per_window = []
         for i in range(args.warmup):
-            pool.map(_ref_sample_worker, [(*sample, i * cores + c) for c in range(cores)])
+            chunk = [[dims[(i * cores + c) % W]] for c in range(cores)]
+            res = pool.map(_ref_window_worker, [(c, HEADS) for c in chunk])
+            per_window.append(max(r[0] for r in res))
+        t_window = max(per_window[-1], 1e-3)
+        budget = 150.0  # seconds of timed work
+        per_proc = max(1, int(budget / (args.steps * t_window)))
+        per_step = min(W, cores * per_proc)
+        cursor = 0
+        done = 0
         start = time.perf_counter()
-        work = 0.0
-        for i in range(args.steps):
-            res = pool.map(_ref_sample_worker, [(*sample, 10_000 + i * cores + c) for c in range(cores)])
-            work += sum(w for _, w in res)
+        for _ in range(args.steps):
+            picks = [dims[(cursor + j) % W] for j in range(per_step)]
+            cursor = (cursor + per_step) % W
+            chunks = [picks[c::cores] for c in range(cores) if picks[c::cores]]
+            res = pool.map(_ref_window_worker, [(c, HEADS) for c in chunks])
+            done += sum(n for _, n in res)
         elapsed = time.perf_counter() - start
-    layer_seconds = elapsed * workload_work / work
-    value = len(lengths) / layer_seconds
-    line = {
+    value = done / elapsed
+    sample = (f"per step {per_step} of the workload's {W} windows ({'the whole layer' if per_step == W else 'the next run of the window list, in rotation'}), "
+              f"split over {cores} processes, each window through the reference's "
+              f"Pack->MMRoPE->WindowAttention->Unpack CPU forward ({HEADS} heads x {HEAD_DIM}, {TEXT} text tokens)")
+    mode = "sharded" if world > 1 else "replicas"
+    return {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed * 1000 / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
-        "config": {"workload": name, "description": desc, "heads": HEADS, "head_dim": HEAD_DIM, "text_tokens": TEXT},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": cpu_kind(),
-                         "sample": f"per step, {cores} processes each run the reference CPU chain on one "
-                                   f"cfg4-shaped window (4x8x8 video + {TEXT} text, {heads} heads); "
-                                   f"scaled to the workload by sum(L^2)*heads"},
+        "scaling": "strong" if mode == "sharded" else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic N(0,1) QKV, seeded", "config": workload_config(name, world, mode),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": cpu_kind(), "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    return line
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -375,12 +426,8 @@ def run_b200(args, rank, world, local_rank):
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": precision, "data": "synthetic N(0,1) QKV, seeded",
-            "config": {"workload": name, "description": desc, "grid": list(grid), "num_windows": list(num),
-                       "shifted": bool(shifted), "windows": W, "heads": HEADS, "head_dim": HEAD_DIM,
-                       "text_tokens": TEXT, "rope_dim": 126, "precision": precision,
-                       "attention_kernel": "tcgen05" if kernel_kind == 1 else "simt",
-                       "l2": f"inputs {in_bytes / 1e9:.2f} GB per step > 126 MB L2; no flush",
-                       "parallelism": f"weak: {world} independent layer(s), one per GPU"},
+            "config": workload_config(name, world),
+            "windows": W, "attention_kernel": "tcgen05" if kernel_kind == 1 else "simt",
             "attn_tflops": round(flops * world / (ms_per_step / 1000.0) / 1e12, 2),
             "gpu_launches": launches,
             "e2e": None if e2e_ms is None else {
@@ -797,9 +844,7 @@ def main():
         line = run_b200(args, rank, world, local_rank)
         if rank == 0:
             if world == 1 and not args.no_cpu_baseline:
-                grid, num, shifted, _, _ = WORKLOADS[args.workload]
-                _, lengths = window_costs(grid, num, shifted)
-                line["cpu_baseline"] = cpu_baseline_single(sum(L * L for L in lengths) * HEADS, len(lengths))
+                line["cpu_baseline"] = cpu_baseline_single(args.workload)
             print(json.dumps(line), flush=True)
     finally:
         if world > 1:

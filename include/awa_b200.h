@@ -173,10 +173,15 @@ int awa_forward(const awa_plan* plan, int precision, int heads, int head_dim, in
  *   - Limit: the layer's workspace (awa_forward_workspace_bytes) must fit in
  *     AWA_NOALLOC_SCRATCH_BYTES, e.g. 56 windows at 58 text tokens, 20 heads,
  *     head_dim 128. Larger layers get AWA_ERR_INVALID and a message; use
- *     awa_forward with a workspace for them.
- *   - The first call on a device looks up the scratch's device address (with
- *     that device current; it must be the plan's device). Make that first
- *     call before any stream capture begins.
+ *     awa_forward with a workspace for them. The check counts fp32 text
+ *     partials, which the fp32 kernel writes; the tensor-core kernel writes
+ *     them as bf16 and would need half, so on that path the limit is
+ *     conservative by a factor of two.
+ *   - Every call looks up the scratch's device address on the current device
+ *     (which must be the plan's device), so a context created anew on the
+ *     device (cudaDeviceReset) is picked up. The first call on a device loads
+ *     the library's device code there: make it before any stream capture
+ *     begins.
  *   - All calls on a GPU share the one scratch array, which keeps the last
  *     call's contents. Nothing in it needs to start at zero (each call writes
  *     every value it later reads), but calls that overlap on the GPU (other
@@ -264,6 +269,19 @@ int awa_out_project(int tokens, int in_dim, int out_dim, const void* x, int64_t 
  * the first device check that failed since the last call (a bounded wait that
  * gave up). Synchronises the device. Clears the flag. */
 int awa_device_status(void);
+
+/* Self-test of the bounded waits that every wait in the library's kernels
+ * uses (no counterpart in the reference). Launches one block of two warps that
+ * wait on mbarriers nothing ever completes -- no copy, MMA or arrival is
+ * issued, so nothing is in flight: the first warp with a limit of limit_us
+ * microseconds (1..1000000), the second with a limit 1000 times longer, which
+ * must end early on the abort flag the first warp raises when it gives up.
+ * Synchronises the stream. *observed (host) gets bit 0 when the first wait
+ * gave up, bit 1 when the second stopped on the abort; 3 is a pass. The give-up
+ * sets the device status flag as a real one does (code 51), so the next
+ * awa_device_status() returns AWA_ERR_DEVICE and clears it; the device stays
+ * usable. */
+int awa_selftest_bounded_wait(unsigned limit_us, int* observed, awa_stream_t stream);
 
 /* Which attention kernel awa_window_attention / awa_forward would launch for
  * these arguments: 1 = tcgen05 (sm_100a tensor cores: AWA_PREC_BF16 with bf16

@@ -4,11 +4,12 @@ Two CPU implementations of the SeedVR2-ncnn AWA chain live here:
 
 * ``Oracle``: the C restatement in ``awa_oracle.c`` (always built).
 * ``Reference``: the reference's own ``src/awa/awa_layers.cpp`` compiled
-  unmodified against ``ncnn_shim/`` (``_ref/libawa_ref.so``; built only where
-  the reference sources exist, then carried with the repository copy).
+  unmodified against the library's ncnn API subset
+  (``seedvr2-ncnn_b200/ncnn_compat/ncnn``; ``_ref/libawa_ref.so``, built only
+  where a reference checkout is given, then carried with the repository copy).
 
-Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg
-import this module; the product never does.
+Only ``tests/``, ``__graft_entry__`` (build and smoke) and ``bench.py``'s
+CPU-baseline and reference legs import this module; the product never does.
 """
 
 from __future__ import annotations
@@ -24,18 +25,24 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "libawa_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libawa_ref.so")
-REFERENCE_ROOT = os.environ.get("SEEDVR2_REFERENCE_ROOT", "/root/reference")
+REF_BATCH_SO = os.path.join(HERE, "_ref", "libawa_ref_batch.so")  # built with NCNN_BATCH=1
+# Root of a reference checkout (its src/awa/awa_layers.cpp is compiled into
+# _ref/); unset means "use the prebuilt _ref/ library if it is there".
+REFERENCE_ROOT = os.environ.get("SEEDVR2_REFERENCE_ROOT", "")
 
 _i = ctypes.c_int
 _p = ctypes.c_void_p
 
 
-def build(reference: bool = True) -> None:
-    """Compile the C restatement, and the reference when its sources exist."""
+def build(reference: bool = True, reference_root: Optional[str] = None) -> None:
+    """Compile the C restatement, and the reference's CPU forward when a
+    reference checkout is given (argument, else SEEDVR2_REFERENCE_ROOT) and
+    holds src/awa/awa_layers.cpp."""
+    root = reference_root or REFERENCE_ROOT
     targets = ["oracle"]
-    if reference and os.path.isfile(os.path.join(REFERENCE_ROOT, "src", "awa", "awa_layers.cpp")):
+    if reference and root and os.path.isfile(os.path.join(root, "src", "awa", "awa_layers.cpp")):
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", HERE, f"REFERENCE={REFERENCE_ROOT}", *targets], check=True)
+    subprocess.run(["make", "-s", "-C", HERE, f"REFERENCE={root}", *targets], check=True)
 
 
 def _ptr(array: Optional[np.ndarray]):
@@ -234,7 +241,9 @@ class Reference:
         lib.ref_chain_seconds.argtypes = [_p, _p]
         lib.ref_layer_forward.restype = _i
         lib.ref_layer_forward.argtypes = [_p, _i, _p, _p, _i, _i, _p, _p]
+        lib.ref_batch_build.restype = _i
         self.lib = lib
+        self.batch_build = bool(lib.ref_batch_build())
 
     @staticmethod
     def available(path: str = REF_SO) -> bool:

@@ -1,7 +1,8 @@
 // ref_driver.cpp -- C entry points around the reference's OWN CPU forward
 // (src/awa/awa_layers.cpp of HGinkgo/SeedVR2-ncnn, compiled unmodified with
-// NCNN_VULKAN=0 against oracle/ncnn_shim). TEST INFRASTRUCTURE: used by tests/
-// to pin the C restatement (awa_oracle.c) and by bench.py's reference arm.
+// NCNN_VULKAN=0 against the library's ncnn API subset in
+// seedvr2-ncnn_b200/ncnn_compat/ncnn). TEST INFRASTRUCTURE: used by tests/ to
+// pin the C restatement (awa_oracle.c) and by bench.py's reference arm.
 //
 // The chain is driven the way an ncnn graph drives it (dit_stack.cpp:180,
 // export_dit_block.py:578-644): layers are created through
@@ -47,7 +48,9 @@ struct RefChain
 //   layout 0: dims 3, w=d, h=3H, c=tokens
 //   layout 1: dims 3, w=d, h=H,  c=3*tokens (all q rows, then k, then v)
 //   layout 2: dims 4, w=d, h=H,  d=3, c=tokens
-void fill_qkv(ncnn::Mat& m, const float* src, int tokens, int heads, int head_dim, int layout)
+//   layout 3: dims 3, w=d, h=H,  c=3, n=tokens (NCNN_BATCH builds only)
+// Returns false for a layout this build does not have.
+bool fill_qkv(ncnn::Mat& m, const float* src, int tokens, int heads, int head_dim, int layout)
 {
     const size_t head_row = (size_t)heads * head_dim;
     if (layout == 0)
@@ -64,20 +67,39 @@ void fill_qkv(ncnn::Mat& m, const float* src, int tokens, int heads, int head_di
                 std::memcpy(m.channel(qkv * tokens + t).data, src + ((size_t)t * 3 + qkv) * head_row,
                             head_row * sizeof(float));
     }
-    else
+    else if (layout == 2)
     {
         m.create(head_dim, heads, 3, tokens, 4u);
         for (int t = 0; t < tokens; t++)
             std::memcpy(m.channel(t).data, src + (size_t)t * 3 * head_row, 3 * head_row * sizeof(float));
     }
+#if NCNN_BATCH
+    else if (layout == 3)
+    {
+        m.create(head_dim, heads, 3, 4u, 1, tokens);
+        for (int t = 0; t < tokens; t++)
+            for (int qkv = 0; qkv < 3; qkv++)
+                std::memcpy(m.batch(t).channel(qkv).data, src + ((size_t)t * 3 + qkv) * head_row,
+                            head_row * sizeof(float));
+    }
+#endif
+    else
+        return false;
+    return true;
 }
 
-// Copy a dims-3 Mat (w, h, c) to a dense [c][h][w] array.
+// Copy a Mat to dense rows: dims 3 (w, h, c) -> [c][h][w]; dims 4 with batch
+// items (the NCNN_BATCH video output, w, h, d, c, n) -> [n][c][d][h][w].
 void read_dense(const ncnn::Mat& m, float* dst)
 {
-    const size_t plane = (size_t)m.w * m.h;
-    for (int c = 0; c < m.c; c++)
-        std::memcpy(dst + (size_t)c * plane, m.channel(c).data, plane * sizeof(float));
+    const size_t plane = (size_t)m.w * m.h * (m.dims == 4 ? m.d : 1);
+    for (int b = 0; b < m.n; b++)
+        for (int c = 0; c < m.c; c++)
+        {
+            const float* src = static_cast<const float*>(m.data) + b * m.nstep + c * m.cstep;
+            std::memcpy(dst, src, plane * sizeof(float));
+            dst += plane;
+        }
 }
 
 double now_seconds()
@@ -88,6 +110,16 @@ double now_seconds()
 } // namespace
 
 extern "C" {
+
+// 1 when the reference was compiled with NCNN_BATCH.
+int ref_batch_build(void)
+{
+#if NCNN_BATCH
+    return 1;
+#else
+    return 0;
+#endif
+}
 
 int ref_make_windows(int source_t, int source_h, int source_w, int num_t, int num_h, int num_w, int shifted,
                      int* out6, int capacity)
@@ -168,8 +200,9 @@ int ref_chain_forward(void* handle, const float* video_qkv, const float* text_qk
     RefChain* chain = static_cast<RefChain*>(handle);
     ncnn::Option opt;
     std::vector<ncnn::Mat> bottoms(2);
-    fill_qkv(bottoms[0], video_qkv, chain->source_tokens, chain->heads, chain->head_dim, chain->layout);
-    fill_qkv(bottoms[1], text_qkv, chain->text_tokens, chain->heads, chain->head_dim, chain->layout);
+    if (!fill_qkv(bottoms[0], video_qkv, chain->source_tokens, chain->heads, chain->head_dim, chain->layout) ||
+        !fill_qkv(bottoms[1], text_qkv, chain->text_tokens, chain->heads, chain->head_dim, chain->layout))
+        return -1;
 
     std::vector<ncnn::Mat> pack_tops;
     double t0 = now_seconds();
@@ -238,8 +271,9 @@ int ref_layer_forward(void* handle, int which, const float* in0, const float* in
     if (which == 0)
     {
         bottoms.resize(2);
-        fill_qkv(bottoms[0], in0, chain->source_tokens, chain->heads, chain->head_dim, chain->layout);
-        fill_qkv(bottoms[1], in1, chain->text_tokens, chain->heads, chain->head_dim, chain->layout);
+        if (!fill_qkv(bottoms[0], in0, chain->source_tokens, chain->heads, chain->head_dim, chain->layout) ||
+            !fill_qkv(bottoms[1], in1, chain->text_tokens, chain->heads, chain->head_dim, chain->layout))
+            return -1;
     }
     else
     {

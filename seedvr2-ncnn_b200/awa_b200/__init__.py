@@ -20,6 +20,7 @@ from typing import List, Optional, Sequence, Tuple
 PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB_PATH = os.path.join(PKG_DIR, "lib", "libawa_b200.so")
 COMPAT_PATH = os.path.join(PKG_DIR, "lib", "libawa_ncnn_compat.so")
+COMPAT_BATCH_PATH = os.path.join(PKG_DIR, "lib", "libawa_ncnn_compat_batch.so")  # built with NCNN_BATCH
 
 AWA_F32 = 0
 AWA_BF16 = 1
@@ -39,7 +40,7 @@ EXPORTED_SYMBOLS = (
     "awa_forward_noalloc",
     "awa_forward_windows", "awa_text_finalize", "awa_scatter_video_shard", "awa_gather_video_shard",
     "awa_window_range_video_rows", "awa_partition_windows", "awa_qkv_project", "awa_out_project", "awa_device_status",
-    "awa_attention_kernel_kind",
+    "awa_selftest_bounded_wait", "awa_attention_kernel_kind",
     "awa_profile_enable", "awa_profile_reset", "awa_profile_collect", "awa_last_error", "awa_version",
     "awa_graph_find_chains", "awa_graph_find_chains_file", "awa_graph_make_dynamic", "awa_manifest_validate",
     "awa_sha256", "awa_sha256_file",
@@ -129,6 +130,7 @@ def library() -> ctypes.CDLL:
         "awa_window_range_video_rows": (i64, [p, i, i]),
         "awa_partition_windows": (i, [p, i, p]),
         "awa_device_status": (i, []),
+        "awa_selftest_bounded_wait": (i, [ctypes.c_uint, ctypes.POINTER(i), p]),
         "awa_attention_kernel_kind": (i, [p, i, i, i, i]),
         "awa_profile_enable": (None, [i]),
         "awa_profile_reset": (None, []),
@@ -550,34 +552,43 @@ def profile_collect() -> dict:
 
 
 # ---------------------------------------------------------------- ncnn layer classes
-_compat = None
+_compat = {}
 
 
-def ncnn_compat() -> ctypes.CDLL:
-    global _compat
-    if _compat is None:
+def ncnn_compat(batch: bool = False) -> ctypes.CDLL:
+    """The ncnn layer classes' library: built against the ncnn API subset
+    without NCNN_BATCH, or (batch=True) with it."""
+    if batch not in _compat:
         library()
-        if not os.path.isfile(COMPAT_PATH):
-            raise ImportError(f"{COMPAT_PATH} is missing")
-        lib = ctypes.CDLL(COMPAT_PATH)
+        path = COMPAT_BATCH_PATH if batch else COMPAT_PATH
+        if not os.path.isfile(path):
+            raise ImportError(f"{path} is missing")
+        lib = ctypes.CDLL(path)
         p, i = ctypes.c_void_p, ctypes.c_int
         lib.awa_ncnn_run_chain.restype = i
         lib.awa_ncnn_run_chain.argtypes = [p, i, i, i, i, i, i, i, p, p, p, p, p, p, p, p]
-        _compat = lib
-    return _compat
+        lib.awa_ncnn_batch_build.restype = i
+        assert bool(lib.awa_ncnn_batch_build()) == batch, path
+        _compat[batch] = lib
+    return _compat[batch]
 
 
 def ncnn_run_chain(params: Sequence[int], heads: int, head_dim: int, video_qkv, text_qkv, layout: int = 0,
-                   runtime_spec: bool = False, bf16: bool = False, device_blobs: bool = False):
+                   runtime_spec: bool = False, bf16: bool = False, device_blobs: bool = False,
+                   batch_build: bool = False):
     """Run SeedVR2AWAPack -> MMRoPE -> WindowAttention -> AWAUnpack through the
     ncnn layer classes (register_seedvr2_awa_layers + Net + ParamDict + forward).
 
     video_qkv / text_qkv: host numpy arrays [tokens, 3, H, d] (float32, or
-    uint16 holding bf16 bits). Returns a dict of dense numpy outputs.
+    uint16 holding bf16 bits), written into QKV blob encoding `layout` (0: w=d,
+    h=3H, c=N; 1: w=d, h=H, c=3N; 2: w=d, h=H, d=3, c=N; 3: w=d, h=H, c=3, n=N,
+    which needs batch_build). batch_build selects the classes built with
+    NCNN_BATCH, whose video output is the 4-D batched blob. Returns a dict of
+    dense numpy outputs (video rows in t, h, w order) and the status.
     """
     import numpy as np
 
-    lib = ncnn_compat()
+    lib = ncnn_compat(batch_build)
     params = list(params)
     elem = 2 if video_qkv.dtype == np.uint16 else 4
     out_np = np.uint16 if bf16 else np.float32

@@ -81,6 +81,7 @@ constexpr uint32_t kColS = 128;  // + 64 * tile
 constexpr uint32_t kColO = 256;  // + 128 * tile
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: healthy waits last microseconds
 constexpr uint64_t kDrainLimitNs = 200000000ull;  // 0.2 s for copies / MMAs in flight at exit
+constexpr int kWaitSelftestCode = 51;                  // error code of the wait self-test
 
 // Tensor maps of one launch, [source][q, k, v] with 128-byte swizzle and
 // 64-feature boxes. Fused: source 0 = video QKV (features x w x h x t, box
@@ -304,7 +305,7 @@ __device__ __forceinline__ uint64_t block_mask(const AttnArgs& a, const Job& job
 // thread sleeps inside try_wait (woken when the phase completes) and checks the
 // abort flag and the time limit only when a sleep expires.
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort, int* error_flag,
-                                         int code)
+                                         int code, uint64_t limit_ns = kWaitLimitNs)
 {
     if (tc::mbar_try_wait(bar, parity))
         return true;
@@ -315,7 +316,7 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
             return true;
         if (*abort)
             return false;
-        if (tc::global_ns() - start > kWaitLimitNs)
+        if (tc::global_ns() - start > limit_ns)
         {
             *abort = 1;
             if (error_flag)
@@ -323,6 +324,33 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
             return false;
         }
     }
+}
+
+// Self-test of wait_bar: two warps wait on mbarriers that nothing completes
+// (no copy, no MMA, no arrival is ever issued, so nothing is in flight when the
+// block exits). Warp 0's wait has a limit of limit_ns and gives up, setting the
+// abort flag and the device error flag; warp 1's wait has a limit 1000 times
+// longer and must stop on the abort flag well before that. observed gets bit 0
+// when warp 0 gave up, bit 1 when warp 1 stopped on the abort.
+__global__ void __launch_bounds__(64) wait_selftest_kernel(uint64_t limit_ns, int* error_flag, int* observed)
+{
+    __shared__ uint64_t bars[2];
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0)
+    {
+        tc::mbar_init(&bars[0], 1);
+        tc::mbar_init(&bars[1], 1);
+        abort_flag = 0;
+        tc::mbar_fence_init();
+    }
+    __syncthreads();
+    const int warp = threadIdx.x / 32;
+    const uint64_t limit = warp == 0 ? limit_ns : limit_ns * 1000;
+    const uint64_t start = tc::global_ns();
+    const bool done = wait_bar(&bars[warp], 0, &abort_flag, warp == 0 ? error_flag : nullptr, kWaitSelftestCode, limit);
+    const uint64_t took = tc::global_ns() - start;
+    if ((threadIdx.x & 31) == 0 && !done)
+        atomicOr(observed, warp == 0 ? 1 : (took < limit ? 2 : 0));
 }
 
 // Bounded wait used on the way out (ignores the abort flag).
@@ -1364,6 +1392,12 @@ int launch_tc(const AttnArgs& a, const TmaMaps& maps, cudaStream_t stream)
 }
 
 }  // namespace
+
+int launch_wait_selftest(uint64_t limit_ns, int* error_flag, int* observed, cudaStream_t stream)
+{
+    wait_selftest_kernel<<<1, 64, 0, stream>>>(limit_ns, error_flag, observed);
+    return (int)cudaGetLastError();
+}
 
 int launch_attention_tc(const AttnArgs& args, int packed, int in_dtype, int out_dtype, cudaStream_t stream)
 {

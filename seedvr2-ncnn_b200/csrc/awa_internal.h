@@ -123,6 +123,8 @@ int launch_shard_copy(const PlanDevice& plan, int heads, int head_dim, int windo
 // Attention: packed != 0 selects packed mode. Template dispatch on dtypes.
 int launch_attention_simt(const AttnArgs& args, int packed, int in_dtype, int out_dtype, cudaStream_t stream);
 int launch_attention_tc(const AttnArgs& args, int packed, int in_dtype, int out_dtype, cudaStream_t stream);
+// The bounded-wait self-test kernel (awa_selftest_bounded_wait).
+int launch_wait_selftest(uint64_t limit_ns, int* error_flag, int* observed, cudaStream_t stream);
 // x W^T with the per-head RMSNorm of Q and K (head_dim 128); arguments checked
 // by the caller.
 int launch_qkv_project(int tokens, int model_dim, int heads, const void* x, int64_t x_stride, const void* w,

@@ -15,7 +15,6 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
-#include <mutex>
 
 namespace
 {
@@ -25,31 +24,23 @@ namespace
 // only a handle for cudaGetSymbolAddress, never a device address.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[AWA_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mutex;
-void* g_scratch_address[kMaxDevices] = {nullptr};  // device address of g_noalloc_scratch, per device
-
-// Device address of the scratch on the current device, looked up once per
-// device (with that device current).
-int scratch_address(int device, void** out)
+// Device address of the scratch on the current device. Looked up on every
+// call: the lookup is cheap once the module is loaded, and a context created
+// anew on the device (after cudaDeviceReset) moves the array, so a cached
+// address could go stale. The first lookup on a device loads the library's
+// device code there, which must not happen inside a stream capture.
+int scratch_address(void** out)
 {
-    if (device < 0 || device >= kMaxDevices)
-        return awa::report_error(AWA_ERR_INVALID, "awa_forward_noalloc: device index out of range");
-    std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (!g_scratch_address[device])
+    void* p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (err != cudaSuccess || !p)
     {
-        void* p = nullptr;
-        const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (err != cudaSuccess || !p)
-        {
-            char message[256];
-            std::snprintf(message, sizeof(message), "awa_forward_noalloc: cudaGetSymbolAddress failed: %s",
-                          cudaGetErrorString(err));
-            return awa::report_error(AWA_ERR_CUDA, message);
-        }
-        g_scratch_address[device] = p;
+        char message[256];
+        std::snprintf(message, sizeof(message), "awa_forward_noalloc: cudaGetSymbolAddress failed: %s",
+                      cudaGetErrorString(err));
+        return awa::report_error(AWA_ERR_CUDA, message);
     }
-    *out = g_scratch_address[device];
+    *out = p;
     return AWA_OK;
 }
 
@@ -85,7 +76,7 @@ extern "C" int awa_forward_noalloc(const awa_plan* plan, int precision, int head
         return awa::report_error(AWA_ERR_INVALID,
                                  "awa_forward_noalloc: the plan's device must be the current device");
     void* scratch = nullptr;
-    rc = scratch_address(device, &scratch);
+    rc = scratch_address(&scratch);
     if (rc)
         return rc;
     // The attention kernel writes every text partial of the call before the

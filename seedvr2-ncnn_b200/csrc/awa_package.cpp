@@ -510,7 +510,10 @@ bool check_grid(const Layer& layer, const AwaParams& p, bool& dynamic, std::stri
 {
     const long long* v = p.value;
     dynamic = v[0] == -1 && v[1] == -1 && v[2] == -1;
-    const bool grid_ok = dynamic || (v[0] > 0 && v[1] > 0 && v[2] > 0 && v[0] * v[1] * v[2] <= INT_MAX);
+    // T*H*W must fit an int; each factor is checked against INT_MAX divided by
+    // the others before any product is formed, so nothing can overflow.
+    const bool grid_ok = dynamic || (v[0] > 0 && v[1] > 0 && v[2] > 0 && v[0] <= INT_MAX / v[1] &&
+                                     v[0] * v[1] <= INT_MAX / v[2]);
     if (!grid_ok || v[3] <= 0 || v[4] <= 0 || v[5] <= 0 || v[6] <= 0)
     {
         error = "invalid AWA grid metadata in " + layer.name() +

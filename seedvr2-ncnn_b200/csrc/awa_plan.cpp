@@ -960,6 +960,29 @@ int awa_partition_windows(const awa_plan* plan, int parts, int* bounds)
     return AWA_OK;
 }
 
+int awa_selftest_bounded_wait(unsigned limit_us, int* observed, awa_stream_t stream)
+{
+    if (limit_us == 0 || limit_us > 1000000u || !observed)
+        return fail(AWA_ERR_INVALID, "awa_selftest_bounded_wait: limit must be 1..1000000 us");
+    int* flag = awa::device_error_flag();
+    if (!flag)
+        return fail(AWA_ERR_CUDA, "device status flag unavailable");
+    int* d_observed = nullptr;
+    cudaError_t err = cudaMalloc(&d_observed, sizeof(int));
+    if (err != cudaSuccess)
+        return cuda_fail(err, "self-test buffer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    err = cudaMemsetAsync(d_observed, 0, sizeof(int), s);
+    if (err == cudaSuccess)
+        err = static_cast<cudaError_t>(awa::launch_wait_selftest((uint64_t)limit_us * 1000ull, flag, d_observed, s));
+    if (err == cudaSuccess)
+        err = cudaMemcpyAsync(observed, d_observed, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess)
+        err = cudaStreamSynchronize(s);
+    cudaFree(d_observed);
+    return err == cudaSuccess ? AWA_OK : cuda_fail(err, "awa_selftest_bounded_wait");
+}
+
 int awa_device_status(void)
 {
     int* flag = awa::device_error_flag();

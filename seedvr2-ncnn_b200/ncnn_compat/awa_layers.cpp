@@ -33,39 +33,48 @@ struct QkvLayout
     int64_t qkv_stride = 0;
 };
 
-// The four QKV blob encodings of describe_qkv_layout (awa_layers.cpp:124-170),
-// for any blob type with ncnn Mat geometry.
+// The QKV blob encodings of describe_qkv_layout (awa_layers.cpp:124-170),
+// for any blob type with ncnn Mat geometry: (w=d, h=3H, c=N), (w=d, h=H,
+// c=3N), (dims 4: w=d, h=H, d=3, c=N) and, in NCNN_BATCH builds, (w=d, h=H,
+// c=3, n=N) with one token per batch item.
 template <typename Blob>
-bool describe_qkv(int dims, int w, int h, int d, int c, size_t cstep, int tokens, QkvLayout& layout)
+bool describe_qkv(const Blob& b, int tokens, QkvLayout& layout)
 {
-    (void)sizeof(Blob);
-    if (w <= 0 || h <= 0)
+    if (b.w <= 0 || b.h <= 0)
         return false;
-    layout.head_dim = w;
-    if (dims == 3)
+    layout.head_dim = b.w;
+    if (b.dims == 3)
     {
-        if (h % 3 == 0 && c == tokens)
+        if (b.h % 3 == 0 && b.c == tokens)
         {
-            layout.heads = h / 3;
-            layout.token_stride = (int64_t)cstep;
-            layout.qkv_stride = (int64_t)layout.heads * w;
+            layout.heads = b.h / 3;
+            layout.token_stride = (int64_t)b.cstep;
+            layout.qkv_stride = (int64_t)layout.heads * b.w;
         }
-        else if (c == tokens * 3)
+        else if (b.c == tokens * 3)
         {
-            layout.heads = h;
-            layout.token_stride = (int64_t)cstep;
-            layout.qkv_stride = (int64_t)tokens * (int64_t)cstep;
+            layout.heads = b.h;
+            layout.token_stride = (int64_t)b.cstep;
+            layout.qkv_stride = (int64_t)tokens * (int64_t)b.cstep;
         }
+#if NCNN_BATCH
+        else if (b.c == 3 && b.n == tokens)
+        {
+            layout.heads = b.h;
+            layout.token_stride = (int64_t)b.nstep;
+            layout.qkv_stride = (int64_t)b.cstep;
+        }
+#endif
         else
             return false;
     }
-    else if (dims == 4)
+    else if (b.dims == 4)
     {
-        if (d != 3 || c != tokens)
+        if (b.d != 3 || b.c != tokens)
             return false;
-        layout.heads = h;
-        layout.token_stride = (int64_t)cstep;
-        layout.qkv_stride = (int64_t)h * w;
+        layout.heads = b.h;
+        layout.token_stride = (int64_t)b.cstep;
+        layout.qkv_stride = (int64_t)b.h * b.w;
     }
     else
         return false;
@@ -74,14 +83,12 @@ bool describe_qkv(int dims, int w, int h, int d, int c, size_t cstep, int tokens
 
 bool describe(const ncnn::Mat& m, int tokens, QkvLayout& layout)
 {
-    return m.elempack == 1 && (m.elemsize == 4u || m.elemsize == 2u) &&
-           describe_qkv<ncnn::Mat>(m.dims, m.w, m.h, m.d, m.c, m.cstep, tokens, layout);
+    return m.elempack == 1 && (m.elemsize == 4u || m.elemsize == 2u) && describe_qkv(m, tokens, layout);
 }
 
 bool describe(const seedvr2::CudaBlob& b, int tokens, QkvLayout& layout)
 {
-    return (b.elemsize == 4u || b.elemsize == 2u) &&
-           describe_qkv<seedvr2::CudaBlob>(b.dims, b.w, b.h, b.d, b.c, b.cstep, tokens, layout);
+    return (b.elemsize == 4u || b.elemsize == 2u) && describe_qkv(b, tokens, layout);
 }
 
 int dtype_of(size_t elemsize)
@@ -89,9 +96,17 @@ int dtype_of(size_t elemsize)
     return elemsize == 2u ? AWA_BF16 : AWA_F32;
 }
 
+// Bytes from a blob's first element to the end of its storage.
+template <typename Blob>
+size_t blob_bytes(const Blob& m)
+{
+    const size_t one = m.dims >= 3 ? m.cstep * m.c : (size_t)m.w * m.h;
+    return (m.n > 1 ? m.nstep * (size_t)(m.n - 1) + one : one) * m.elemsize;
+}
+
 size_t mat_bytes(const ncnn::Mat& m)
 {
-    return m.dims >= 3 ? m.cstep * m.c * m.elemsize : (size_t)m.w * m.h * m.elemsize;
+    return blob_bytes(m);
 }
 
 size_t align16(size_t bytes)
@@ -134,7 +149,7 @@ std::vector<AwaWindow> make_awa_windows(int source_t, int source_h, int source_w
     return out;
 }
 
-int cuda_blob_create(CudaBlob& blob, int dims, int w, int h, int d, int c, size_t elemsize)
+int cuda_blob_create(CudaBlob& blob, int dims, int w, int h, int d, int c, size_t elemsize, int n)
 {
     cuda_blob_free(blob);
     blob.dims = dims;
@@ -142,9 +157,13 @@ int cuda_blob_create(CudaBlob& blob, int dims, int w, int h, int d, int c, size_
     blob.h = h;
     blob.d = d;
     blob.c = c;
+    blob.n = n;
     blob.elemsize = elemsize;
     blob.cstep = dims >= 3 ? align16((size_t)w * h * d * elemsize) / elemsize : (size_t)w * h;
-    const size_t bytes = align16(blob.cstep * (dims >= 3 ? c : 1) * elemsize);
+    blob.nstep = blob.cstep * (dims >= 3 ? c : 1);
+    if (n > 1)
+        blob.nstep = ((blob.nstep * elemsize + 4095) & ~(size_t)4095) / elemsize;
+    const size_t bytes = align16(blob.nstep * (size_t)n * elemsize);
     if (bytes == 0 || cudaMalloc(&blob.data, bytes) != cudaSuccess)
     {
         blob.data = nullptr;
@@ -489,6 +508,62 @@ int SeedVR2AWAUnpack::load_param(const ncnn::ParamDict& pd)
     return load_common_params(pd, 126);
 }
 
+namespace
+{
+
+// The video output of Unpack. Without NCNN_BATCH it is (w=d, h=H, c=N_v):
+// one token per channel, cstep apart. With NCNN_BATCH it is the 4-D batched
+// blob (w=d, h=H, d=W, c=H_grid, n=T) of awa_layers.cpp:655-656, token
+// (t, y, x) at t*nstep + y*cstep + x*H*d: tokens are evenly strided inside a
+// frame when cstep is W*H*d, and frames are nstep apart, which the 4 KiB batch
+// alignment can make more than a frame's size. awa_unpack writes one token
+// stride, so frames that are not evenly strided go through a dense staging
+// buffer and a pitched copy per frame.
+struct VideoTarget
+{
+    int64_t token_stride = 0;  // stride for awa_unpack when writing in place
+    bool in_place = true;      // else: dense staging, then copy_frames()
+};
+
+template <typename Blob>
+VideoTarget video_target(const Blob& out, int heads, int head_dim, const awa_plan_info& info)
+{
+    VideoTarget t;
+    const int64_t row = (int64_t)heads * head_dim;
+#if NCNN_BATCH
+    const bool rows_even = out.cstep == (size_t)row * info.source_w;
+    const bool frames_even = out.nstep == out.cstep * (size_t)info.source_h;
+    t.in_place = rows_even && (frames_even || info.source_t == 1);
+    t.token_stride = row;
+#else
+    (void)row;
+    (void)info;
+    t.token_stride = (int64_t)out.cstep;
+#endif
+    return t;
+}
+
+// Dense [N_v][H*d] rows at src -> the batched video blob at dst, one pitched
+// copy per frame (rows of one grid line are contiguous in both).
+template <typename Blob>
+cudaError_t copy_frames(void* dst, const Blob& out, const void* src, int heads, int head_dim,
+                        const awa_plan_info& info, cudaMemcpyKind kind, cudaStream_t stream)
+{
+    const size_t es = out.elemsize;
+    const size_t line = (size_t)heads * head_dim * info.source_w * es;
+    for (int t = 0; t < info.source_t; t++)
+    {
+        const unsigned char* s = static_cast<const unsigned char*>(src) + (size_t)t * info.source_h * line;
+        unsigned char* d = static_cast<unsigned char*>(dst) + (size_t)t * out.nstep * es;
+        const cudaError_t err = cudaMemcpy2DAsync(d, out.cstep * es, s, line, line, info.source_h, kind, stream);
+        if (err != cudaSuccess)
+            return err;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace
+
 int SeedVR2AWAUnpack::forward(const std::vector<ncnn::Mat>& bottom_blobs, std::vector<ncnn::Mat>& top_blobs,
                               const ncnn::Option& opt) const
 {
@@ -505,22 +580,17 @@ int SeedVR2AWAUnpack::forward(const std::vector<ncnn::Mat>& bottom_blobs, std::v
 #if NCNN_BATCH
     top_blobs[0].create(head_dim, heads, info_.source_w, info_.source_h, out_elem, 1, info_.source_t,
                         opt.blob_allocator);
-    if (!top_blobs[0].empty() && top_blobs[0].cstep != (size_t)head_dim * heads * info_.source_w)
-        return -1;  // tokens must be evenly strided
 #else
     top_blobs[0].create(head_dim, heads, info_.source_tokens, out_elem, opt.blob_allocator);
 #endif
     top_blobs[1].create(head_dim, heads, info_.text_tokens, out_elem, opt.blob_allocator);
     if (top_blobs[0].empty() || top_blobs[1].empty())
         return -100;
-#if NCNN_BATCH
-    const int64_t video_token_stride = (int64_t)head_dim * heads;
-#else
-    const int64_t video_token_stride = (int64_t)top_blobs[0].cstep;
-#endif
+    const VideoTarget target = video_target(top_blobs[0], heads, head_dim, info_);
     std::lock_guard<std::mutex> lock(mutex_);
     void* din = staging(0, mat_bytes(packed));
-    void* dv = staging(1, mat_bytes(top_blobs[0]));
+    void* dv = staging(1, target.in_place ? mat_bytes(top_blobs[0])
+                                          : (size_t)info_.source_tokens * heads * head_dim * out_elem);
     void* dt = staging(2, mat_bytes(top_blobs[1]));
     if (!din || !dv || !dt)
         return -100;
@@ -528,9 +598,11 @@ int SeedVR2AWAUnpack::forward(const std::vector<ncnn::Mat>& bottom_blobs, std::v
     int rc = AWA_OK;
     if (err == cudaSuccess)
         rc = awa_unpack(plan_, heads, head_dim, dtype_of(packed.elemsize), din, (int64_t)packed.cstep,
-                        dtype_of(out_elem), dv, video_token_stride, dt, (int64_t)top_blobs[1].cstep, nullptr);
+                        dtype_of(out_elem), dv, target.token_stride, dt, (int64_t)top_blobs[1].cstep, nullptr);
     if (err == cudaSuccess && rc == AWA_OK)
-        err = download(top_blobs[0], dv);
+        err = target.in_place ? download(top_blobs[0], dv)
+                              : copy_frames(top_blobs[0].data, top_blobs[0], dv, heads, head_dim, info_,
+                                            cudaMemcpyDeviceToHost, nullptr);
     if (err == cudaSuccess && rc == AWA_OK)
         err = download(top_blobs[1], dt);
     return finish(err, rc, "SeedVR2AWAUnpack");
@@ -549,14 +621,34 @@ int SeedVR2AWAUnpack::forward_cuda(const std::vector<CudaBlob>& bottom_blobs, st
     const int head_dim = packed.w;
     const size_t out_elem = opt.use_bf16_storage ? 2u : 4u;
     top_blobs.resize(2);
-    if (seedvr2::cuda_blob_create(top_blobs[0], 3, head_dim, heads, 1, info_.source_tokens, out_elem) ||
-        seedvr2::cuda_blob_create(top_blobs[1], 3, head_dim, heads, 1, info_.text_tokens, out_elem))
+#if NCNN_BATCH
+    const int video_rc = seedvr2::cuda_blob_create(top_blobs[0], 4, head_dim, heads, info_.source_w,
+                                                   info_.source_h, out_elem, info_.source_t);
+#else
+    const int video_rc = seedvr2::cuda_blob_create(top_blobs[0], 3, head_dim, heads, 1, info_.source_tokens, out_elem);
+#endif
+    if (video_rc || seedvr2::cuda_blob_create(top_blobs[1], 3, head_dim, heads, 1, info_.text_tokens, out_elem))
         return -100;
-    return to_ncnn_status(awa_unpack(plan_, heads, head_dim, dtype_of(packed.elemsize), packed.data,
-                                     (int64_t)packed.cstep, dtype_of(out_elem), top_blobs[0].data,
-                                     (int64_t)top_blobs[0].cstep, top_blobs[1].data, (int64_t)top_blobs[1].cstep,
-                                     opt.stream),
-                          "SeedVR2AWAUnpack");
+    const VideoTarget target = video_target(top_blobs[0], heads, head_dim, info_);
+    void* dv = top_blobs[0].data;
+    if (!target.in_place)
+    {
+        std::lock_guard<std::mutex> lock(mutex_);
+        dv = staging(5, (size_t)info_.source_tokens * heads * head_dim * out_elem);
+        if (!dv)
+            return -100;
+    }
+    int rc = awa_unpack(plan_, heads, head_dim, dtype_of(packed.elemsize), packed.data, (int64_t)packed.cstep,
+                        dtype_of(out_elem), dv, target.token_stride, top_blobs[1].data, (int64_t)top_blobs[1].cstep,
+                        opt.stream);
+    if (rc == AWA_OK && !target.in_place &&
+        copy_frames(top_blobs[0].data, top_blobs[0], dv, heads, head_dim, info_, cudaMemcpyDeviceToDevice,
+                    static_cast<cudaStream_t>(opt.stream)) != cudaSuccess)
+    {
+        std::fprintf(stderr, "SeedVR2AWAUnpack: batched video copy failed\n");
+        return -1;
+    }
+    return to_ncnn_status(rc, "SeedVR2AWAUnpack");
 }
 
 // ------------------------------------------------------------------ registration

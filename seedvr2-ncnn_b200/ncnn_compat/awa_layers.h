@@ -70,11 +70,15 @@ struct CudaBlob
     int c = 0;
     size_t elemsize = 4;
     size_t cstep = 0;
+    int n = 1;         // batch items (NCNN_BATCH layouts)
+    size_t nstep = 0;  // elements between batch items
     bool owned = false;  // allocated by a layer (release with cuda_blob_free)
 };
 
-// Layout-compatible with ncnn::Mat::create: cstep aligned to 16 bytes for dims >= 3.
-int cuda_blob_create(CudaBlob& blob, int dims, int w, int h, int d, int c, size_t elemsize);
+// Layout-compatible with ncnn::Mat::create: cstep aligned to 16 bytes for
+// dims >= 3; with n > 1 (the batched form) nstep is cstep * c rounded up to
+// 4 KiB, as the Mat subset in ncnn_compat/ncnn does.
+int cuda_blob_create(CudaBlob& blob, int dims, int w, int h, int d, int c, size_t elemsize, int n = 1);
 void cuda_blob_free(CudaBlob& blob);
 
 struct CudaOption

@@ -17,8 +17,9 @@ namespace
 {
 
 // Dense [tokens][3][H][d] host array -> QKV blob in encoding `layout`
-// (0: w=d,h=3H,c=N; 1: w=d,h=H,c=3N; 2: dims 4, w=d,h=H,d=3,c=N).
-void fill_qkv(ncnn::Mat& m, const void* src, int tokens, int heads, int head_dim, int layout, size_t elemsize)
+// (0: w=d,h=3H,c=N; 1: w=d,h=H,c=3N; 2: dims 4, w=d,h=H,d=3,c=N; 3, NCNN_BATCH
+// builds only: w=d,h=H,c=3,n=N, one token per batch item).
+bool fill_qkv(ncnn::Mat& m, const void* src, int tokens, int heads, int head_dim, int layout, size_t elemsize)
 {
     const size_t row = (size_t)heads * head_dim * elemsize;
     const unsigned char* s = static_cast<const unsigned char*>(src);
@@ -35,41 +36,82 @@ void fill_qkv(ncnn::Mat& m, const void* src, int tokens, int heads, int head_dim
             for (int t = 0; t < tokens; t++)
                 std::memcpy(m.channel(q * tokens + t).data, s + ((size_t)t * 3 + q) * row, row);
     }
-    else
+    else if (layout == 2)
     {
         m.create(head_dim, heads, 3, tokens, elemsize);
         for (int t = 0; t < tokens; t++)
             std::memcpy(m.channel(t).data, s + (size_t)t * 3 * row, 3 * row);
     }
+#if NCNN_BATCH
+    else if (layout == 3)
+    {
+        m.create(head_dim, heads, 3, elemsize, 1, tokens);
+        for (int t = 0; t < tokens; t++)
+            for (int q = 0; q < 3; q++)
+                std::memcpy(m.batch(t).channel(q).data, s + ((size_t)t * 3 + q) * row, row);
+    }
+#endif
+    else
+        return false;
+    return true;
 }
 
+// Any blob with Mat geometry -> dense host rows. dims 3: [c][h][w];
+// dims 4 (with batch items n): [n][c][d][h][w].
 void read_dense(const ncnn::Mat& m, void* dst)
 {
+    unsigned char* out = static_cast<unsigned char*>(dst);
+    if (m.dims < 3)
+    {
+        std::memcpy(out, m.data, (size_t)m.w * m.h * m.elemsize);
+        return;
+    }
     const size_t plane = (size_t)m.w * m.h * m.elemsize;
-    for (int c = 0; c < m.c; c++)
-        std::memcpy(static_cast<unsigned char*>(dst) + (size_t)c * plane, m.channel(c).data, plane);
+    const int depth = m.dims == 4 ? m.d : 1;
+    for (int b = 0; b < m.n; b++)
+        for (int c = 0; c < m.c; c++)
+        {
+            const unsigned char* src = static_cast<const unsigned char*>(m.data) + (b * m.nstep + c * m.cstep) * m.elemsize;
+            std::memcpy(out, src, plane * depth);
+            out += plane * depth;
+        }
 }
 
+size_t storage_bytes(int dims, int w, int h, int c, int n, size_t cstep, size_t nstep, size_t elemsize)
+{
+    const size_t one = dims >= 3 ? cstep * c : (size_t)w * h;
+    return (n > 1 ? nstep * (size_t)(n - 1) + one : one) * elemsize;
+}
+
+// Device blob -> host Mat of the same geometry (cstep / nstep kept).
 ncnn::Mat to_mat(const seedvr2::CudaBlob& b)
 {
     ncnn::Mat m;
     if (b.dims == 1)
         m.create(b.w, b.elemsize);
+    else if (b.dims == 4 && b.n > 1)
+        m.create(b.w, b.h, b.d, b.c, b.elemsize, 1, b.n);
+    else if (b.dims == 4)
+        m.create(b.w, b.h, b.d, b.c, b.elemsize);
     else
         m.create(b.w, b.h, b.c, b.elemsize);
-    cudaMemcpy(m.data, b.data, m.dims == 1 ? (size_t)b.w * b.elemsize : b.cstep * b.c * b.elemsize,
+    if (m.cstep != b.cstep || (b.n > 1 && m.nstep != b.nstep))
+        return ncnn::Mat();
+    cudaMemcpy(m.data, b.data, storage_bytes(b.dims, b.w, b.h, b.c, b.n, b.cstep, b.nstep, b.elemsize),
                cudaMemcpyDeviceToHost);
     return m;
 }
 
+// Host Mat -> device blob of the same geometry.
 seedvr2::CudaBlob to_blob(const ncnn::Mat& m)
 {
     seedvr2::CudaBlob b;
-    seedvr2::cuda_blob_create(b, m.dims, m.w, m.h, m.d, m.c, m.elemsize);
+    seedvr2::cuda_blob_create(b, m.dims, m.w, m.h, m.d, m.c, m.elemsize, m.n);
     if (b.data)
-        cudaMemcpy(b.data, m.data, m.dims >= 3 ? m.cstep * m.c * m.elemsize : (size_t)m.w * m.h * m.elemsize,
+        cudaMemcpy(b.data, m.data, storage_bytes(m.dims, m.w, m.h, m.c, m.n, m.cstep, m.nstep, m.elemsize),
                    cudaMemcpyHostToDevice);
     b.cstep = m.cstep;
+    b.nstep = m.nstep;
     return b;
 }
 
@@ -77,10 +119,22 @@ seedvr2::CudaBlob to_blob(const ncnn::Mat& m)
 
 extern "C" {
 
+// 1 when this library was built with NCNN_BATCH (batched QKV and video blobs).
+int awa_ncnn_batch_build(void)
+{
+#if NCNN_BATCH
+    return 1;
+#else
+    return 0;
+#endif
+}
+
 // params: ParamDict ids 0-8. Inputs are dense host arrays of elemsize bytes per
-// element (4 = fp32, 2 = bf16). device_blobs != 0 runs forward_cuda on device
-// copies. Outputs (dense, output element size = 2 when bf16 else 4) may be NULL.
-// Returns the first non-zero layer status.
+// element (4 = fp32, 2 = bf16), written into the QKV blob encoding `layout`
+// (see fill_qkv; 3 needs a library built with NCNN_BATCH). device_blobs != 0
+// runs forward_cuda on device copies. Outputs (dense, output element size = 2
+// when bf16 else 4) may be NULL. Returns the first non-zero layer status, -1
+// for a layout this build does not have.
 int awa_ncnn_run_chain(const int* params, int heads, int head_dim, int layout, int use_runtime_spec, int bf16,
                        int device_blobs, int input_elemsize, const void* video_qkv, const void* text_qkv,
                        void* packed, float* cu_seqlens, void* roped, void* attended, void* video_out, void* text_out)
@@ -116,9 +170,10 @@ int awa_ncnn_run_chain(const int* params, int heads, int head_dim, int layout, i
         ncnn::Option opt;
         opt.use_bf16_storage = bf16 != 0;
         std::vector<ncnn::Mat> in(2), t0, t1, t2, t3;
-        fill_qkv(in[0], video_qkv, video_tokens, heads, head_dim, layout, (size_t)input_elemsize);
-        fill_qkv(in[1], text_qkv, params[6], heads, head_dim, layout, (size_t)input_elemsize);
-        if (!device_blobs)
+        if (!fill_qkv(in[0], video_qkv, video_tokens, heads, head_dim, layout, (size_t)input_elemsize) ||
+            !fill_qkv(in[1], text_qkv, params[6], heads, head_dim, layout, (size_t)input_elemsize))
+            rc = -1;
+        else if (!device_blobs)
         {
             rc = layers[0]->forward(in, t0, opt);
             std::vector<ncnn::Mat> r_in(1, rc == 0 ? t0[0] : ncnn::Mat());

@@ -2,7 +2,12 @@
 // refcounted storage, cstep aligned to 16 bytes for dims >= 3, channel() /
 // row() / depth() / batch() views aliasing the parent. The AWA layers are
 // compiled against real ncnn in an ncnn build; this subset lets them build and
-// run standalone (the reference's ncnn submodule is empty).
+// run standalone (the reference's ncnn submodule is empty). The parity oracle
+// compiles the reference's own CPU forward against the same headers.
+//
+// Batched Mats (n > 1, the NCNN_BATCH layouts) keep each batch item's storage
+// on a 4 KiB boundary: nstep is cstep * c rounded up to 4096 bytes, so a
+// batch stride is not in general c channel strides.
 #pragma once
 
 #include <cstddef>
@@ -46,7 +51,12 @@ public:
     {
         create_impl(4, _w, _h, _d, _c, _elemsize, 1, 1);
     }
-    // Batched form used under NCNN_BATCH (w, h, d, c, elemsize, elempack, n).
+    // Batched forms used under NCNN_BATCH: (w, h, c, elemsize, elempack, n) and
+    // (w, h, d, c, elemsize, elempack, n).
+    void create(int _w, int _h, int _c, size_t _elemsize, int _elempack, int _n, Allocator* = 0)
+    {
+        create_impl(3, _w, _h, 1, _c, _elemsize, _elempack, _n);
+    }
     void create(int _w, int _h, int _d, int _c, size_t _elemsize, int _elempack, int _n, Allocator* = 0)
     {
         create_impl(4, _w, _h, _d, _c, _elemsize, _elempack, _n);
@@ -199,6 +209,8 @@ private:
         else
             cstep = (size_t)w * h;
         nstep = cstep * c;
+        if (n > 1)
+            nstep = ((nstep * elemsize + 4095) & ~(size_t)4095) / elemsize;
         const size_t bytes = align16(nstep * n * elemsize);
         if (bytes == 0)
             return;

@@ -2,7 +2,7 @@
 
 Run in a container that has the reference checkout (read-only is fine):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 It imports ``tools/reference/{seedvr2_baseline,awa_attention,dit_block}.py`` of
 HGinkgo/SeedVR2-ncnn and records, for each configuration:
@@ -138,7 +138,7 @@ def make_out_fixture(torch) -> None:
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="root of a reference checkout")
     parser.add_argument("--only", choices=["gemms"], default=None)
     args = parser.parse_args()
     sys.path.insert(0, args.reference)

@@ -3,7 +3,7 @@ normalize_dynamic_awa_template (tools/export_dit_block.py:38-124).
 
 Run in a container that has the reference checkout (read-only is fine):
 
-    python tests/golden/make_param_golden.py --reference /root/reference
+    python tests/golden/make_param_golden.py --reference <reference checkout>
 
 Each case is an ncnn .param text built here (block graphs shaped the way the
 exporter writes its AWA lines, tools/export_dit_block.py:578-644, plus broken
@@ -109,7 +109,7 @@ def cases():
 
 def main():
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="root of a reference checkout")
     args = parser.parse_args()
     sys.path.insert(0, args.reference)
     from tools.export_dit_block import normalize_dynamic_awa_template  # noqa: E402

@@ -5,8 +5,10 @@ layer in seconds:
   test_library_host.py);
 * Pack and MMRoPE are bit-exact over the full layer (checked here by hashing
   against the oracle's per-window restatement on sampled windows);
-* attention of sampled windows (a full one, a short one, edge windows of the
-  shifted layer) against the oracle run on exactly those windows;
+* attention of at least 16 sampled windows -- one of every window shape
+  (each clipped edge class of the shifted and non-divisible layers), the
+  longest and shortest, and windows spread over the layer -- against the
+  oracle run on exactly those windows: video rows and each window's text rows;
 * the fused chain against the layer-by-layer chain over the whole layer
   (video rows and the text mean over all windows).
 """
@@ -29,15 +31,36 @@ from awa_b200 import AWA_PREC_BF16, AWA_PREC_FP32  # noqa: E402
 FULL = [
     ("cfg4", LayerConfig(21, 64, 64, 6, 8, 8, shifted=0), AWA_PREC_BF16),
     ("cfg4-shifted", LayerConfig(21, 64, 64, 6, 8, 8, shifted=1), AWA_PREC_BF16),
+    # BASELINE's "1344 windows": 1x8x8 windows of the same grid
+    ("cfg4b", LayerConfig(21, 64, 64, 21, 8, 8, shifted=0), AWA_PREC_BF16),
+    ("cfg4b-shifted", LayerConfig(21, 64, 64, 21, 8, 8, shifted=1), AWA_PREC_BF16),
+    # adaptive windows on 9x45x80 (3x8x8, 3x5x8 at the bottom edge)
+    ("cfg5", LayerConfig(9, 45, 80, 3, 6, 10, shifted=0), AWA_PREC_BF16),
+    ("cfg5-shifted", LayerConfig(9, 45, 80, 3, 6, 10, shifted=1), AWA_PREC_BF16),
+    ("cfg5-fp32", LayerConfig(9, 45, 80, 3, 6, 10, shifted=0), AWA_PREC_FP32),
     ("cfg5-fp32-shifted", LayerConfig(9, 45, 80, 3, 6, 10, shifted=1), AWA_PREC_FP32),
 ]
 
+MIN_SAMPLES = 16
 
-def sample_windows(cu: np.ndarray):
+
+def sample_windows(windows, cu: np.ndarray):
+    """At least MIN_SAMPLES windows: one of every window shape (each clipped
+    edge class of a shifted or non-divisible layer), the first, last, longest
+    and shortest, then windows spread evenly over the list."""
+    count = len(windows)
     lengths = np.diff(cu)
-    count = len(lengths)
-    picks = {0, count - 1, int(np.argmax(lengths)), int(np.argmin(lengths)), count // 2}
-    return sorted(picks)
+    picks = {0, count - 1, int(np.argmax(lengths)), int(np.argmin(lengths))}
+    shapes = {}
+    for i, (t0, t1, h0, h1, w0, w1) in enumerate(windows):
+        shapes.setdefault((t1 - t0, h1 - h0, w1 - w0), i)
+    picks.update(shapes.values())
+    step = max(1, count // MIN_SAMPLES)
+    i = step // 2
+    while len(picks) < min(MIN_SAMPLES, count):
+        picks.add(i % count)
+        i += step
+    return sorted(picks), len(shapes)
 
 
 @pytest.mark.parametrize("name,cfg,precision", FULL, ids=[f[0] for f in FULL])
@@ -54,11 +77,22 @@ def test_full_layer(name, cfg, precision, oracle):
     packed32, _ = plan.pack(v.float(), t.float())
     roped32 = plan.mmrope(packed32)
 
-    # Sampled windows: oracle Pack + MMRoPE + attention on exactly those windows.
+    # Sampled windows: oracle Pack + MMRoPE + attention on exactly those windows,
+    # against the fused chain's video rows and its per-window text rows (the
+    # text partials it leaves in the workspace, in window order).
     table = oracle.rope_table(cfg)
-    video, _ = plan.forward(v, t, precision, out_dtype=torch.float32)
+    workspace = torch.empty(plan.workspace_bytes(cfg.heads, cfg.head_dim), dtype=torch.uint8, device="cuda")
+    video, _ = plan.forward(v, t, precision, out_dtype=torch.float32, workspace=workspace)
+    torch.cuda.synchronize()
+    tc = plan.attention_kernel_kind(precision, cfg.heads, cfg.head_dim, dtype) == 1
+    rows_per_window = cfg.text_tokens * cfg.heads * cfg.head_dim
+    partials = (workspace.view(torch.bfloat16) if tc else workspace.view(torch.float32))[
+        : plan.info.window_count * rows_per_window].view(plan.info.window_count, cfg.text_tokens, cfg.heads,
+                                                          cfg.head_dim)
     tol = BF16_REL_L2 if precision == AWA_PREC_BF16 else FP32_REL_L2
-    for w in sample_windows(cu):
+    picks, shapes = sample_windows(maps["windows"], cu)
+    assert len(picks) >= min(MIN_SAMPLES, len(cu) - 1) and shapes >= 1
+    for w in picks:
         rows = np.arange(cu[w], cu[w + 1])
         seq = maps["sequence_index"][rows]
         seq_t = torch.from_numpy(seq.astype(np.int64)).cuda()
@@ -75,7 +109,8 @@ def test_full_layer(name, cfg, precision, oracle):
                                threads=8)
         vrows = seq[seq < cfg.source_tokens]
         ours = to_host(video[torch.from_numpy(vrows.astype(np.int64)).cuda()])
-        assert rel_l2(ours, att_w[: len(vrows)]) < tol, (name, w)
+        assert rel_l2(ours, att_w[: len(vrows)]) < tol, (name, w, "video")
+        assert rel_l2(to_host(partials[w]), att_w[len(vrows):]) < tol, (name, w, "text")
 
     # Whole layer: fused chain == layer chain (same precision), video and text.
     attended = plan.window_attention(roped32.to(dtype), precision, out_dtype=torch.float32)

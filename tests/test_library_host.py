@@ -40,9 +40,11 @@ def test_library_exports_every_declared_symbol():
     assert b"sm_100a" in lib.awa_version()
 
 
-def test_ncnn_compat_library_loads():
-    lib = awa_b200.ncnn_compat()
+@pytest.mark.parametrize("batch", [False, True], ids=["plain", "ncnn-batch"])
+def test_ncnn_compat_library_loads(batch):
+    lib = awa_b200.ncnn_compat(batch)
     assert hasattr(lib, "awa_ncnn_run_chain")
+    assert lib.awa_ncnn_batch_build() == int(batch)
 
 
 with open(os.path.join(GOLDEN, "windows.json")) as _f:

@@ -124,6 +124,29 @@ def test_chain_bitexact_with_compiled_reference(oracle, reference, cfg, layout):
         assert np.array_equal(ours[key], ref[key]), key
 
 
+@pytest.mark.parametrize("cfg", [c for c in REF_CHAIN_CASES if c.rope_dim and c.head_dim < 128] + REF_CHAIN_CASES[3:4],
+                         ids=lambda c: f"{c.source_t}x{c.source_h}x{c.source_w}-s{c.shifted}")
+def test_ncnn_batch_reference_build(oracle, cfg):
+    """The reference compiled with NCNN_BATCH=1 (describe_qkv_layout's c=3,
+    n=N branch, awa_layers.cpp:142-149; the 4-D batched video output of
+    :655-656 and :668-670): on the batched QKV encoding it gives the same values
+    as the C restatement, and on the other encodings too."""
+    from oracle.oracle import REF_BATCH_SO, Reference
+
+    if not Reference.available(REF_BATCH_SO):
+        pytest.skip("oracle/_ref/libawa_ref_batch.so not built")
+    ref = Reference(REF_BATCH_SO)
+    assert ref.batch_build
+    rng = np.random.default_rng(11 + cfg.source_tokens)
+    v = rng.standard_normal((cfg.source_tokens, 3, cfg.heads, cfg.head_dim), dtype=np.float32)
+    t = rng.standard_normal((cfg.text_tokens, 3, cfg.heads, cfg.head_dim), dtype=np.float32)
+    ours = oracle.chain(cfg, v, t, threads=2)
+    for layout in (3, 0):
+        got = ref.chain(cfg, v, t, layout=layout)
+        for key in ("packed", "cu_seqlens", "roped", "attended", "video", "text"):
+            assert np.array_equal(ours[key], got[key]), (layout, key)
+
+
 def test_reference_rejects_bad_rope_dim(reference):
     handle, status = reference.create(LayerConfig(1, 4, 4, 1, 2, 2, text_tokens=2, rope_dim=125, heads=1, head_dim=128))
     assert not handle and status == -1

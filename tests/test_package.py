@@ -190,6 +190,12 @@ BAD_GRAPHS = {
                      "invalid AWA grid metadata in awa_pack"),
     "missing text tokens": ("roped attended 0=1 1=16 2=16 3=1 4=8 5=8 6=58", "roped attended 0=1 1=16 2=16 3=1 4=8 5=8",
                             "invalid AWA grid metadata in awa_attention"),
+    # three grid values that each fit an int but whose product is near 2^93:
+    # the T*H*W <= INT_MAX rule must hold without the product overflowing
+    "grid product overflow": ("awa_cu_seqlens 0=1 1=16 2=16", "awa_cu_seqlens 0=2147483647 1=2147483646 2=2147483645",
+                              "invalid AWA grid metadata in awa_pack"),
+    "grid product just past int": ("awa_cu_seqlens 0=1 1=16 2=16", "awa_cu_seqlens 0=2 1=32768 2=32768",
+                                   "invalid AWA grid metadata in awa_pack"),
     "float parameter": ("8=126", "8=126.0", "parameter 8 of mmrope is not an integer"),
     "rope dim": ("8=126", "8=125", "invalid rope dimension 125 in mmrope"),
     "duplicate id": ("8=126", "8=126 5=8", "duplicate AWA parameter 5 in mmrope"),
