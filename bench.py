@@ -257,6 +257,178 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- B200 arm
+def measured_peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, source) from MEASURED_PEAKS.json, else the
+    profiling recipe's fallback figures."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+        return float(peaks["hbm_gbs"]), float(peaks["bf16_tflops"]), "measured"
+    except (OSError, ValueError, KeyError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def clock_device(local_rank):
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    return int(visible.split(",")[local_rank]) if visible else local_rank
+
+
+def run_sharded(args, rank, world, local_rank):
+    """One layer split over the N ranks (awa_forward_sharded: window ranges of
+    near-equal cost, or head ranges when windows are few; NCCL all-reduce of the
+    text partial sums and all-gather of the video rows). Strong scaling: the
+    whole layer is one step at every N."""
+    import torch
+    import torch.distributed as dist
+
+    import awa_b200
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    name = args.workload
+    grid, num, shifted, precision, desc = WORKLOADS[name]
+    prec = awa_b200.AWA_PREC_BF16 if precision == "bf16" else awa_b200.AWA_PREC_FP32
+    dtype = torch.bfloat16 if precision == "bf16" else torch.float32
+    esize = 2 if precision == "bf16" else 4
+    wins, lengths = window_costs(grid, num, shifted)
+    W = len(lengths)
+    flops = attention_flops(lengths)
+    n_v = grid[0] * grid[1] * grid[2]
+    plan = awa_b200.AwaPlan(*grid, *num, text_tokens=TEXT, shifted=bool(shifted))
+    box = [awa_b200.AwaComm.unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    comm = awa_b200.AwaComm(box[0], world, rank)
+    by_heads, bounds = plan.shard_split(world, HEADS)
+
+    gen = torch.Generator(device=device).manual_seed(1234)  # the same layer on every rank
+    video_qkv = torch.randn(n_v, 3, HEADS, HEAD_DIM, device=device, generator=gen).to(dtype)
+    text_qkv = torch.randn(TEXT, 3, HEADS, HEAD_DIM, device=device, generator=gen).to(dtype)
+    video_out = torch.empty(n_v, HEADS, HEAD_DIM, device=device, dtype=dtype)
+    text_out = torch.empty(TEXT, HEADS, HEAD_DIM, device=device, dtype=dtype)
+    workspace = torch.empty(plan.sharded_workspace_bytes(world, HEADS, HEAD_DIM, dtype), device=device,
+                            dtype=torch.uint8)
+    stream = torch.cuda.current_stream(device)
+
+    def step(v=video_qkv, t=text_qkv):
+        plan.forward_sharded(comm, v, t, prec, out_dtype=dtype, workspace=workspace, video_out=video_out,
+                             text_out=text_out, stream=stream)
+
+    def barrier():
+        dist.barrier(device_ids=[local_rank])
+
+    clocks = ClockSampler(clock_device(local_rank))
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    awa_b200.device_status()
+    awa_b200.profile_reset()
+    awa_b200.profile_enable(True)
+    barrier()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    stop.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    awa_b200.profile_enable(False)
+    prof = awa_b200.profile_collect()
+    kernel_ms = sum(v[1] for v in prof.values()) / args.steps  # this rank's library kernels per step
+    attn_name = next((k for k in prof if k.startswith("awa_attention")), None)
+    attn_ms = prof.get(attn_name, (1, 0.0))[1] / max(prof.get(attn_name, (1, 0.0))[0], 1)
+    t = torch.tensor([start.elapsed_time(stop), kernel_ms * args.steps], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_step = float(t[0].item()) / args.steps
+    compute_ms_max = float(t[1].item()) / args.steps
+    value = W / (ms_per_step / 1000.0)
+
+    # end to end with host buffers: each rank copies its 1/N slice of the
+    # replicated QKV from pinned host memory, NCCL all-gathers the slices (every
+    # rank needs every row, as the ncnn boundary hands the layer whole inputs),
+    # runs the sharded layer, and copies its 1/N slice of the (replicated) video
+    # output back; rank 0 also copies the text output.
+    e2e_ms, e2e_steps = None, 0
+    in_bytes = (n_v + TEXT) * 3 * HEADS * HEAD_DIM * esize
+    out_bytes = (n_v + TEXT) * HEADS * HEAD_DIM * esize
+    if not args.no_e2e:
+        e2e_steps = max(3, min(args.steps, args.e2e_steps))
+        per = -(-n_v // world)
+        lo, hi = min(rank * per, n_v), min((rank + 1) * per, n_v)
+        host_v = torch.empty(per, 3, HEADS, HEAD_DIM, dtype=dtype, pin_memory=True)
+        host_v[: hi - lo].copy_(video_qkv[lo:hi])
+        host_t = torch.empty(text_qkv.shape, dtype=dtype, pin_memory=True)
+        host_t.copy_(text_qkv)
+        host_o = torch.empty(per, HEADS, HEAD_DIM, dtype=dtype, pin_memory=True)
+        host_ot = torch.empty(text_out.shape, dtype=dtype, pin_memory=True)
+        gathered = torch.empty(per * world, 3, HEADS, HEAD_DIM, dtype=dtype, device=device)
+        slot = torch.empty(per, 3, HEADS, HEAD_DIM, dtype=dtype, device=device)
+        dev_t = torch.empty_like(text_qkv)
+
+        def e2e_step():
+            slot.copy_(host_v, non_blocking=True)
+            dev_t.copy_(host_t, non_blocking=True)
+            dist.all_gather_into_tensor(gathered, slot)
+            step(gathered[:n_v], dev_t)
+            host_o[: hi - lo].copy_(video_out[lo:hi], non_blocking=True)
+            if rank == 0:
+                host_ot.copy_(text_out, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        te = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = float(te.item()) / e2e_steps
+    clock = clocks.stop()
+    awa_b200.device_status()
+    comm.destroy()
+
+    hbm_peak, tensor_peak, peak_src = measured_peaks()
+    if by_heads:
+        share_rows, share_frac = n_v, (bounds[rank + 1] - bounds[rank]) / HEADS
+    else:
+        share_rows = plan.range_video_rows(bounds[rank], bounds[rank + 1])
+        share_frac = 1.0
+    share_heads = HEADS * share_frac
+    alg_bytes = int((share_rows + TEXT) * 4 * share_heads * HEAD_DIM * esize)
+    achieved = alg_bytes / (attn_ms / 1000.0) / 1e9 if attn_ms > 0 else 0.0
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": precision, "data": "synthetic N(0,1) QKV, seeded",
+            "config": workload_config(name, world, "sharded"),
+            "windows": W, "attn_tflops": round(flops / (ms_per_step / 1000.0) / 1e12, 2),
+            "sharded": {"split": "heads" if by_heads else "windows", "bounds": bounds,
+                        "compute_ms_max": round(compute_ms_max, 5),
+                        "collective_and_copies_ms": round(ms_per_step - compute_ms_max, 5),
+                        "kernel_only_value": round(W / (compute_ms_max / 1000.0), 2)},
+            "gpu_launches": sum(v[0] for v in prof.values()),
+            "e2e": None if e2e_ms is None else {
+                "value": round(W / (e2e_ms / 1000.0), 2), "unit": UNIT, "h2d_bytes_per_step": in_bytes,
+                "d2h_bytes_per_step": out_bytes, "steps": e2e_steps, "ms_per_step": round(e2e_ms, 4),
+                "how": "each rank copies 1/N of the QKV rows in and 1/N of the video rows out; NCCL all-gathers "
+                       "the input slices on the device"},
+            "roofline": {"bound": "hbm", "kernel": attn_name, "achieved": round(achieved, 1), "peak": hbm_peak,
+                         "unit": "GB/s", "frac": round(achieved / hbm_peak, 4), "traffic": None,
+                         "peak_source": peak_src, "algorithmic_bytes": alg_bytes, "kernel_ms": round(attn_ms, 5),
+                         "note": "rank 0's share of the layer"},
+            "clocks": clock,
+            "profile": {k: {"launches": v[0], "ms": round(v[1], 4)} for k, v in prof.items()},
+        }
+    return line
+
+
 def run_b200(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -806,6 +978,9 @@ def main():
     parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
     parser.add_argument("--workload", default="cfg4", choices=sorted(WORKLOADS))
     parser.add_argument("--e2e-steps", type=int, default=20)
+    parser.add_argument("--mode", default=None, choices=["sharded", "replicas"],
+                        help="N > 1: sharded (default) splits one layer over the N GPUs with NCCL (strong scaling); "
+                             "replicas runs an independent layer per GPU (weak scaling)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiler captures)")
     parser.add_argument("--stage", default="awa", choices=["awa", "qkv-proj", "out-proj", "stack", "layers"],
@@ -841,7 +1016,8 @@ def main():
             if rank == 0:
                 print(json.dumps(line), flush=True)
             return
-        line = run_b200(args, rank, world, local_rank)
+        mode = args.mode or ("sharded" if world > 1 else "replicas")
+        line = (run_sharded if mode == "sharded" else run_b200)(args, rank, world, local_rank)
         if rank == 0:
             if world == 1 and not args.no_cpu_baseline:
                 line["cpu_baseline"] = cpu_baseline_single(args.workload)

@@ -225,6 +225,44 @@ int64_t awa_window_range_video_rows(const awa_plan* plan, int window_begin, int 
  * attention cost (sum of L^2); bounds receives parts+1 window indices. */
 int awa_partition_windows(const awa_plan* plan, int parts, int* bounds);
 
+/* ---- One layer split over the GPUs of a node.
+ * Windows are independent (SeedVR2WindowAttention::forward,
+ * awa_layers.cpp:1062-1120); the only coupling is the text mean
+ * text += packed / window_count (SeedVR2AWAUnpack::forward :684-685). Each rank
+ * computes a share of the layer and NCCL finishes it, so every rank ends with
+ * the full outputs the ncnn boundary hands on:
+ *   - window split: contiguous window ranges of near-equal attention cost
+ *     (awa_partition_windows); the ranks' video rows are all-gathered and
+ *     scattered to source order, the fp32 text partial sums all-reduced;
+ *   - head split, when there are fewer than 4 windows per rank: each rank runs
+ *     every window for a range of heads; the head slices of the video and text
+ *     outputs are all-gathered.
+ * No kernel reads a peer's memory; NCCL moves the data. libnccl.so.2 is
+ * loaded on first use (inside a PyTorch process: the NCCL torch loaded). */
+typedef struct awa_comm awa_comm;
+
+/* ncclGetUniqueId: rank 0 calls it and hands the bytes (128) to every rank. */
+int awa_comm_unique_id(unsigned char* id, size_t capacity);
+/* ncclCommInitRank on the current device; collective over the nranks ranks. */
+int awa_comm_create(const unsigned char* id, size_t id_bytes, int nranks, int rank, awa_comm** out);
+/* Uses the caller's own ncclComm_t (not destroyed by awa_comm_destroy). */
+int awa_comm_wrap(void* nccl_comm, awa_comm** out);
+void awa_comm_destroy(awa_comm* comm);
+int awa_comm_info(const awa_comm* comm, int* rank, int* nranks);
+/* The split awa_forward_sharded uses for nranks ranks: *by_heads (0/1) and
+ * nranks+1 bounds (window indices, or head indices for a head split). */
+int awa_shard_split(const awa_plan* plan, int nranks, int heads, int* by_heads, int* bounds);
+size_t awa_forward_sharded_workspace_bytes(const awa_plan* plan, int nranks, int heads, int head_dim, int out_dtype);
+/* awa_forward over the ranks of `comm`: same arguments and outputs (on every
+ * rank: inputs replicated, outputs complete), plus a workspace of
+ * awa_forward_sharded_workspace_bytes(). Every rank must call it with the same
+ * plan parameters; the collectives are enqueued on `stream`. */
+int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int heads, int head_dim, int in_dtype,
+                        const void* video_qkv, int64_t video_token_stride, int64_t video_qkv_stride,
+                        const void* text_qkv, int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype,
+                        void* video_out, int64_t video_token_stride_out, void* text_out,
+                        int64_t text_token_stride_out, void* workspace, size_t workspace_bytes, awa_stream_t stream);
+
 /* The producer of the AWA input (the block's QKV projection with the per-head
  * RMSNorm of Q and K), on the tensor cores. Replaces, for one branch (video or
  * text) of a DiT block, proj_qkv + norm_q + norm_k of

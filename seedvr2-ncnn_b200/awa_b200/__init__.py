@@ -41,6 +41,8 @@ EXPORTED_SYMBOLS = (
     "awa_forward_windows", "awa_text_finalize", "awa_scatter_video_shard", "awa_gather_video_shard",
     "awa_window_range_video_rows", "awa_partition_windows", "awa_qkv_project", "awa_out_project", "awa_device_status",
     "awa_selftest_bounded_wait", "awa_attention_kernel_kind",
+    "awa_comm_unique_id", "awa_comm_create", "awa_comm_wrap", "awa_comm_destroy", "awa_comm_info", "awa_shard_split",
+    "awa_forward_sharded_workspace_bytes", "awa_forward_sharded",
     "awa_profile_enable", "awa_profile_reset", "awa_profile_collect", "awa_last_error", "awa_version",
     "awa_graph_find_chains", "awa_graph_find_chains_file", "awa_graph_make_dynamic", "awa_manifest_validate",
     "awa_sha256", "awa_sha256_file",
@@ -131,6 +133,14 @@ def library() -> ctypes.CDLL:
         "awa_partition_windows": (i, [p, i, p]),
         "awa_device_status": (i, []),
         "awa_selftest_bounded_wait": (i, [ctypes.c_uint, ctypes.POINTER(i), p]),
+        "awa_comm_unique_id": (i, [p, sz]),
+        "awa_comm_create": (i, [p, sz, i, i, ctypes.POINTER(p)]),
+        "awa_comm_wrap": (i, [p, ctypes.POINTER(p)]),
+        "awa_comm_destroy": (None, [p]),
+        "awa_comm_info": (i, [p, ctypes.POINTER(i), ctypes.POINTER(i)]),
+        "awa_shard_split": (i, [p, i, i, ctypes.POINTER(i), p]),
+        "awa_forward_sharded_workspace_bytes": (sz, [p, i, i, i, i]),
+        "awa_forward_sharded": (i, [p, p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p, sz, p]),
         "awa_attention_kernel_kind": (i, [p, i, i, i, i]),
         "awa_profile_enable": (None, [i]),
         "awa_profile_reset": (None, []),
@@ -375,6 +385,43 @@ class AwaPlan:
                                            out.data_ptr(), out.stride(0), _stream_ptr(stream)))
         return out
 
+    # ---------------------------------------------------------------- multi-GPU
+    def shard_split(self, nranks: int, heads: int) -> Tuple[bool, List[int]]:
+        """(by_heads, bounds): how awa_forward_sharded splits this layer over
+        nranks ranks -- window bounds, or head bounds when windows are few."""
+        by_heads = ctypes.c_int(0)
+        bounds = (ctypes.c_int * (nranks + 1))()
+        _check(library().awa_shard_split(self._handle, nranks, heads, ctypes.byref(by_heads),
+                                         ctypes.cast(bounds, ctypes.c_void_p)))
+        return bool(by_heads.value), list(bounds)
+
+    def sharded_workspace_bytes(self, nranks: int, heads: int, head_dim: int, out_dtype) -> int:
+        code = out_dtype if isinstance(out_dtype, int) else _dtype_code_of(out_dtype)
+        return int(library().awa_forward_sharded_workspace_bytes(self._handle, nranks, heads, head_dim, code))
+
+    def forward_sharded(self, comm: "AwaComm", video_qkv, text_qkv, precision=AWA_PREC_BF16, out_dtype=None,
+                        workspace=None, video_out=None, text_out=None, stream=None):
+        """awa_forward over the ranks of `comm` (every rank passes the full
+        inputs and gets the full outputs): (video, text)."""
+        torch = _torch()
+        heads, hd = video_qkv.shape[2], video_qkv.shape[3]
+        dt = video_qkv.dtype if out_dtype is None else out_dtype
+        if video_out is None:
+            video_out = torch.empty(self.info.source_tokens, heads, hd, dtype=dt, device=video_qkv.device)
+        if text_out is None:
+            text_out = torch.empty(self.info.text_tokens, heads, hd, dtype=dt, device=video_qkv.device)
+        if workspace is None:
+            need = self.sharded_workspace_bytes(comm.nranks, heads, hd, dt)
+            workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=video_qkv.device)
+        vts, vqs = _qkv_strides(video_qkv)
+        tts, tqs = _qkv_strides(text_qkv)
+        _check(library().awa_forward_sharded(self._handle, comm.handle, precision, heads, hd, _dtype_code(video_qkv),
+                                             video_qkv.data_ptr(), vts, vqs, text_qkv.data_ptr(), tts, tqs,
+                                             _dtype_code(video_out), video_out.data_ptr(), video_out.stride(0),
+                                             text_out.data_ptr(), text_out.stride(0), workspace.data_ptr(),
+                                             workspace.numel() * workspace.element_size(), _stream_ptr(stream)))
+        return video_out, text_out
+
     def partition(self, parts: int) -> List[int]:
         bounds = (ctypes.c_int * (parts + 1))()
         _check(library().awa_partition_windows(self._handle, parts, ctypes.cast(bounds, ctypes.c_void_p)))
@@ -522,6 +569,43 @@ class StackGraph:
         if handle and _lib is not None:
             _lib.awa_stack_graph_destroy(handle)
             self._handle = None
+
+
+def _dtype_code_of(torch_dtype) -> int:
+    torch = _torch()
+    return AWA_BF16 if torch_dtype == torch.bfloat16 else AWA_F32
+
+
+class AwaComm:
+    """An NCCL communicator for awa_forward_sharded (one rank per GPU, on the
+    current device). Every rank passes the same 128-byte id, made once by
+    AwaComm.unique_id() on rank 0 and handed to the others by the caller."""
+
+    def __init__(self, unique_id: bytes, nranks: int, rank: int):
+        handle = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(bytes(unique_id), len(unique_id))
+        _check(library().awa_comm_create(ctypes.cast(buf, ctypes.c_void_p), len(unique_id), nranks, rank,
+                                         ctypes.byref(handle)))
+        self._handle = handle
+        self.nranks, self.rank = nranks, rank
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        _check(library().awa_comm_unique_id(ctypes.cast(buf, ctypes.c_void_p), 128))
+        return buf.raw
+
+    @property
+    def handle(self):
+        return self._handle
+
+    def destroy(self) -> None:
+        if getattr(self, "_handle", None) and _lib is not None:
+            _lib.awa_comm_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        self.destroy()
 
 
 def device_status() -> None:
@@ -675,7 +759,7 @@ def sha256_file(path) -> str:
     return buf.value.decode()
 
 
-__all__ = ["AwaPlan", "AwaError", "PlanInfo", "library", "make_windows", "device_status", "ncnn_run_chain",
+__all__ = ["AwaPlan", "AwaComm", "AwaError", "PlanInfo", "library", "make_windows", "device_status", "ncnn_run_chain",
            "EXPORTED_SYMBOLS", "qkv_project", "out_project", "graph_find_chains", "graph_find_chains_file",
            "graph_make_dynamic", "manifest_validate", "sha256", "sha256_file", "AwaStack", "StackGraph", "StackIO",
            "AWA_STACK_BEFORE", "AWA_STACK_AFTER", "AWA_F32", "AWA_BF16", "AWA_PREC_FP32", "AWA_PREC_BF16"]

@@ -1,0 +1,447 @@
+// awa_shard.cpp -- one AWA layer split over the GPUs of a node
+// (include/awa_b200.h: awa_comm_*, awa_forward_sharded).
+//
+// Windows are independent (SeedVR2WindowAttention::forward runs each window on
+// its own, awa_layers.cpp:1062-1120); the only coupling between them is the
+// text mean text[i] = sum_w attended_text(w)[i] / W (awa_layers.cpp:684-685).
+// So each rank computes a share of the layer and two collectives finish it:
+//
+//   window split (enough windows): rank r runs the fused forward on a
+//     contiguous range of windows of near-equal attention cost, packs its
+//     video rows into its slot of a gather buffer, NCCL all-gathers the slots
+//     (in place), all-reduces the fp32 text partial sums and scatters the other
+//     ranks' rows into its own video output;
+//   head split (fewer than 4 windows per rank): rank r runs the whole layer for
+//     a range of heads -- the QKV and output pointers offset by the first head,
+//     the row strides unchanged -- and the all-gather moves head slices of the
+//     video and text outputs.
+//
+// Every rank ends with the full video and text outputs, as the ncnn boundary
+// requires. NCCL moves the data into local memory: no kernel reads a peer's
+// memory and nothing uses TMA multicast. libnccl.so.2 is opened at run time,
+// so the library loads on machines without NCCL; inside a PyTorch process the
+// dynamic loader hands back the NCCL that torch already loaded.
+#include "awa_b200.h"
+#include "awa_internal.h"
+
+#include <dlfcn.h>
+
+#include <nccl.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+namespace
+{
+
+// ---------------------------------------------------------------- NCCL entry points
+struct Nccl
+{
+    ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*comm_count)(const ncclComm_t, int*) = nullptr;
+    ncclResult_t (*comm_user_rank)(const ncclComm_t, int*) = nullptr;
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+    ncclResult_t (*group_start)() = nullptr;
+    ncclResult_t (*group_end)() = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+    bool ok = false;
+};
+
+const Nccl* nccl()
+{
+    static Nccl n;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h)
+            h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h)
+            return;
+        auto sym = [h](auto& fn, const char* name) {
+            fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
+            return fn != nullptr;
+        };
+        n.ok = sym(n.get_unique_id, "ncclGetUniqueId") && sym(n.comm_init_rank, "ncclCommInitRank") &&
+               sym(n.comm_destroy, "ncclCommDestroy") && sym(n.comm_count, "ncclCommCount") &&
+               sym(n.comm_user_rank, "ncclCommUserRank") && sym(n.all_gather, "ncclAllGather") &&
+               sym(n.all_reduce, "ncclAllReduce") && sym(n.group_start, "ncclGroupStart") &&
+               sym(n.group_end, "ncclGroupEnd") && sym(n.error_string, "ncclGetErrorString");
+    });
+    return n.ok ? &n : nullptr;
+}
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...)
+{
+    char message[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(message, sizeof(message), fmt, ap);
+    va_end(ap);
+    return awa::report_error(code, message);
+}
+
+int nccl_status(const Nccl* n, ncclResult_t r, const char* what)
+{
+    if (r == ncclSuccess)
+        return AWA_OK;
+    return fail(AWA_ERR_CUDA, "%s: %s", what, n->error_string(r));
+}
+
+int cuda_status(cudaError_t e, const char* what)
+{
+    if (e == cudaSuccess)
+        return AWA_OK;
+    return fail(AWA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+size_t align256(size_t v)
+{
+    return (v + 255) & ~(size_t)255;
+}
+
+size_t dsize(int dtype)
+{
+    return dtype == AWA_BF16 ? 2 : 4;
+}
+
+}  // namespace
+
+struct awa_comm
+{
+    ncclComm_t comm = nullptr;
+    int rank = 0;
+    int nranks = 1;
+    int device = -1;
+    bool owned = false;
+};
+
+namespace
+{
+
+// How one layer is split over the ranks of a communicator.
+struct Split
+{
+    bool by_heads = false;
+    std::vector<int> bounds;  // window bounds (nranks + 1) or head bounds (nranks + 1)
+    int64_t slot_rows = 0;    // window split: rows of one rank's slot of the gather buffer
+};
+
+Split make_split(const awa_plan* plan, const awa_plan_info& info, int nranks, int heads)
+{
+    Split s;
+    s.bounds.assign(nranks + 1, 0);
+    s.by_heads = nranks > 1 && info.window_count < 4 * nranks && heads >= nranks;
+    if (s.by_heads)
+    {
+        for (int r = 0; r <= nranks; r++)
+            s.bounds[r] = (int)((int64_t)heads * r / nranks);
+        return s;
+    }
+    awa_partition_windows(plan, nranks, s.bounds.data());
+    for (int r = 0; r < nranks; r++)
+        s.slot_rows = std::max<int64_t>(s.slot_rows, awa_window_range_video_rows(plan, s.bounds[r], s.bounds[r + 1]));
+    return s;
+}
+
+// Workspace layout of awa_forward_sharded (offsets in bytes, each 256-aligned).
+struct Layout
+{
+    size_t text_sum = 0, forward = 0, gather = 0, text_gather = 0, total = 0;
+};
+
+Layout make_layout(const awa_plan* plan, const awa_plan_info& info, const Split& s, int nranks, int heads,
+                   int head_dim, int out_dtype)
+{
+    Layout l;
+    const size_t row = (size_t)heads * head_dim;
+    size_t off = 0;
+    l.text_sum = off;
+    off += align256((size_t)info.text_tokens * row * sizeof(float));
+    l.forward = off;
+    if (s.by_heads)
+    {
+        int most = 0;
+        for (int r = 0; r < nranks; r++)
+            most = std::max(most, s.bounds[r + 1] - s.bounds[r]);
+        off += align256(awa_forward_workspace_bytes(plan, most, head_dim));
+        l.gather = off;
+        // slots of [N_v][most heads][d] video rows, then [T][most heads][d] text rows
+        off += align256((size_t)nranks * info.source_tokens * most * head_dim * dsize(out_dtype));
+        l.text_gather = off;
+        off += align256((size_t)nranks * info.text_tokens * most * head_dim * dsize(out_dtype));
+    }
+    else
+    {
+        int most = 0;
+        for (int r = 0; r < nranks; r++)
+            most = std::max(most, s.bounds[r + 1] - s.bounds[r]);
+        off += align256((size_t)std::max(most, 1) * info.text_tokens * row * sizeof(float));
+        l.gather = off;
+        off += align256((size_t)nranks * std::max<int64_t>(s.slot_rows, 1) * row * dsize(out_dtype));
+        l.text_gather = off;
+    }
+    l.total = off;
+    return l;
+}
+
+}  // namespace
+
+extern "C" {
+
+int awa_comm_unique_id(unsigned char* id, size_t capacity)
+{
+    const Nccl* n = nccl();
+    if (!n)
+        return fail(AWA_ERR_CUDA, "awa_comm_unique_id: libnccl.so.2 could not be loaded");
+    if (!id || capacity < sizeof(ncclUniqueId))
+        return fail(AWA_ERR_INVALID, "awa_comm_unique_id: needs %zu bytes", sizeof(ncclUniqueId));
+    ncclUniqueId uid;
+    int rc = nccl_status(n, n->get_unique_id(&uid), "ncclGetUniqueId");
+    if (rc == AWA_OK)
+        std::memcpy(id, &uid, sizeof(uid));
+    return rc;
+}
+
+int awa_comm_create(const unsigned char* id, size_t id_bytes, int nranks, int rank, awa_comm** out)
+{
+    if (!out)
+        return fail(AWA_ERR_INVALID, "awa_comm_create: NULL output");
+    *out = nullptr;
+    const Nccl* n = nccl();
+    if (!n)
+        return fail(AWA_ERR_CUDA, "awa_comm_create: libnccl.so.2 could not be loaded");
+    if (!id || id_bytes < sizeof(ncclUniqueId) || nranks <= 0 || rank < 0 || rank >= nranks)
+        return fail(AWA_ERR_INVALID, "awa_comm_create: invalid id, rank %d or nranks %d", rank, nranks);
+    awa_comm* c = new awa_comm();
+    if (cudaGetDevice(&c->device) != cudaSuccess)
+    {
+        delete c;
+        return fail(AWA_ERR_CUDA, "awa_comm_create: no current device");
+    }
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, sizeof(uid));
+    const int rc = nccl_status(n, n->comm_init_rank(&c->comm, nranks, uid, rank), "ncclCommInitRank");
+    if (rc != AWA_OK)
+    {
+        delete c;
+        return rc;
+    }
+    c->rank = rank;
+    c->nranks = nranks;
+    c->owned = true;
+    *out = c;
+    return AWA_OK;
+}
+
+int awa_comm_wrap(void* nccl_comm, awa_comm** out)
+{
+    if (!out || !nccl_comm)
+        return fail(AWA_ERR_INVALID, "awa_comm_wrap: NULL communicator");
+    *out = nullptr;
+    const Nccl* n = nccl();
+    if (!n)
+        return fail(AWA_ERR_CUDA, "awa_comm_wrap: libnccl.so.2 could not be loaded");
+    awa_comm* c = new awa_comm();
+    c->comm = static_cast<ncclComm_t>(nccl_comm);
+    int rc = nccl_status(n, n->comm_count(c->comm, &c->nranks), "ncclCommCount");
+    if (rc == AWA_OK)
+        rc = nccl_status(n, n->comm_user_rank(c->comm, &c->rank), "ncclCommUserRank");
+    if (rc == AWA_OK && cudaGetDevice(&c->device) != cudaSuccess)
+        rc = fail(AWA_ERR_CUDA, "awa_comm_wrap: no current device");
+    if (rc != AWA_OK)
+    {
+        delete c;
+        return rc;
+    }
+    *out = c;
+    return AWA_OK;
+}
+
+void awa_comm_destroy(awa_comm* comm)
+{
+    if (!comm)
+        return;
+    const Nccl* n = nccl();
+    if (comm->owned && comm->comm && n)
+        n->comm_destroy(comm->comm);
+    delete comm;
+}
+
+int awa_comm_info(const awa_comm* comm, int* rank, int* nranks)
+{
+    if (!comm)
+        return fail(AWA_ERR_INVALID, "awa_comm_info: NULL communicator");
+    if (rank)
+        *rank = comm->rank;
+    if (nranks)
+        *nranks = comm->nranks;
+    return AWA_OK;
+}
+
+int awa_shard_split(const awa_plan* plan, int nranks, int heads, int* by_heads, int* bounds)
+{
+    awa_plan_info info;
+    if (!plan || nranks <= 0 || heads <= 0 || awa_plan_get_info(plan, &info) != AWA_OK)
+        return fail(AWA_ERR_INVALID, "awa_shard_split: invalid arguments");
+    const Split s = make_split(plan, info, nranks, heads);
+    if (by_heads)
+        *by_heads = s.by_heads ? 1 : 0;
+    if (bounds)
+        std::copy(s.bounds.begin(), s.bounds.end(), bounds);
+    return AWA_OK;
+}
+
+size_t awa_forward_sharded_workspace_bytes(const awa_plan* plan, int nranks, int heads, int head_dim, int out_dtype)
+{
+    awa_plan_info info;
+    if (!plan || nranks <= 0 || heads <= 0 || head_dim <= 0 || awa_plan_get_info(plan, &info) != AWA_OK)
+        return 0;
+    const Split s = make_split(plan, info, nranks, heads);
+    return make_layout(plan, info, s, nranks, heads, head_dim, out_dtype).total;
+}
+
+int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int heads, int head_dim, int in_dtype,
+                        const void* video_qkv, int64_t video_token_stride, int64_t video_qkv_stride,
+                        const void* text_qkv, int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype,
+                        void* video_out, int64_t video_token_stride_out, void* text_out,
+                        int64_t text_token_stride_out, void* workspace, size_t workspace_bytes, awa_stream_t stream)
+{
+    awa_plan_info info;
+    if (!plan || !comm || awa_plan_get_info(plan, &info) != AWA_OK)
+        return fail(AWA_ERR_INVALID, "awa_forward_sharded: NULL plan or communicator");
+    if (heads <= 0 || head_dim <= 0 || !video_qkv || !text_qkv || !video_out || !text_out || !workspace ||
+        (out_dtype != AWA_F32 && out_dtype != AWA_BF16))
+        return fail(AWA_ERR_INVALID, "awa_forward_sharded: invalid arguments");
+    int device = -1;
+    if (cudaGetDevice(&device) != cudaSuccess || device != comm->device || device != info.device)
+        return fail(AWA_ERR_INVALID, "awa_forward_sharded: plan, communicator and current device differ");
+    const Nccl* n = nccl();
+    if (!n)
+        return fail(AWA_ERR_CUDA, "awa_forward_sharded: libnccl.so.2 could not be loaded");
+    const int R = comm->nranks, r = comm->rank;
+    const Split s = make_split(plan, info, R, heads);
+    const Layout l = make_layout(plan, info, s, R, heads, head_dim, out_dtype);
+    if (workspace_bytes < l.total)
+        return fail(AWA_ERR_INVALID, "awa_forward_sharded: workspace of %zu bytes needed, %zu given", l.total,
+                    workspace_bytes);
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t osz = dsize(out_dtype), isz = dsize(in_dtype);
+    const ncclDataType_t otype = out_dtype == AWA_BF16 ? ncclBfloat16 : ncclFloat32;
+    const int64_t row = (int64_t)heads * head_dim;
+    int rc = AWA_OK;
+
+    if (s.by_heads)
+    {
+        // This rank's heads [h0, h1) over every window: offset pointers, same strides.
+        const int h0 = s.bounds[r], hn = s.bounds[r + 1] - s.bounds[r];
+        int most = 0;
+        for (int q = 0; q < R; q++)
+            most = std::max(most, s.bounds[q + 1] - s.bounds[q]);
+        const size_t hoff_in = (size_t)h0 * head_dim * isz, hoff_out = (size_t)h0 * head_dim * osz;
+        if (hn > 0)
+            rc = awa_forward(plan, precision, hn, head_dim, in_dtype,
+                             static_cast<const unsigned char*>(video_qkv) + hoff_in, video_token_stride,
+                             video_qkv_stride, static_cast<const unsigned char*>(text_qkv) + hoff_in,
+                             text_token_stride, text_qkv_stride, out_dtype,
+                             static_cast<unsigned char*>(video_out) + hoff_out, video_token_stride_out,
+                             static_cast<unsigned char*>(text_out) + hoff_out, text_token_stride_out,
+                             ws + l.forward, l.gather - l.forward, stream);
+        if (rc)
+            return rc;
+        // Pack this rank's head slices into its slots ([N_v][most][d] and [T][most][d]).
+        const size_t vslot = (size_t)info.source_tokens * most * head_dim, tslot = (size_t)info.text_tokens * most * head_dim;
+        unsigned char* vg = ws + l.gather;
+        unsigned char* tg = ws + l.text_gather;
+        const size_t width = (size_t)hn * head_dim * osz, spitch = (size_t)most * head_dim * osz;
+        if (hn > 0)
+        {
+            rc = cuda_status(cudaMemcpy2DAsync(vg + r * vslot * osz, spitch,
+                                               static_cast<unsigned char*>(video_out) + hoff_out,
+                                               video_token_stride_out * osz, width, info.source_tokens,
+                                               cudaMemcpyDeviceToDevice, st),
+                             "head slice pack (video)");
+            if (rc == AWA_OK)
+                rc = cuda_status(cudaMemcpy2DAsync(tg + r * tslot * osz, spitch,
+                                                   static_cast<unsigned char*>(text_out) + hoff_out,
+                                                   text_token_stride_out * osz, width, info.text_tokens,
+                                                   cudaMemcpyDeviceToDevice, st),
+                                 "head slice pack (text)");
+        }
+        if (rc)
+            return rc;
+        rc = nccl_status(n, n->group_start(), "ncclGroupStart");
+        if (rc == AWA_OK)
+            rc = nccl_status(n, n->all_gather(vg + r * vslot * osz, vg, vslot, otype, comm->comm, st), "ncclAllGather (video)");
+        if (rc == AWA_OK)
+            rc = nccl_status(n, n->all_gather(tg + r * tslot * osz, tg, tslot, otype, comm->comm, st), "ncclAllGather (text)");
+        const int end_rc = nccl_status(n, n->group_end(), "ncclGroupEnd");
+        rc = rc ? rc : end_rc;
+        if (rc)
+            return rc;
+        for (int q = 0; q < R && rc == AWA_OK; q++)
+        {
+            const int qn = s.bounds[q + 1] - s.bounds[q];
+            if (q == r || qn == 0)
+                continue;
+            const size_t qoff = (size_t)s.bounds[q] * head_dim * osz, qwidth = (size_t)qn * head_dim * osz;
+            rc = cuda_status(cudaMemcpy2DAsync(static_cast<unsigned char*>(video_out) + qoff,
+                                               video_token_stride_out * osz, vg + q * vslot * osz, spitch, qwidth,
+                                               info.source_tokens, cudaMemcpyDeviceToDevice, st),
+                             "head slice unpack (video)");
+            if (rc == AWA_OK)
+                rc = cuda_status(cudaMemcpy2DAsync(static_cast<unsigned char*>(text_out) + qoff,
+                                                   text_token_stride_out * osz, tg + q * tslot * osz, spitch, qwidth,
+                                                   info.text_tokens, cudaMemcpyDeviceToDevice, st),
+                                 "head slice unpack (text)");
+        }
+        return rc;
+    }
+
+    // Window split: this rank's windows [w0, w1).
+    const int w0 = s.bounds[r], w1 = s.bounds[r + 1];
+    float* text_sum = reinterpret_cast<float*>(ws + l.text_sum);
+    rc = awa_forward_windows(plan, precision, heads, head_dim, w0, w1, in_dtype, video_qkv, video_token_stride,
+                             video_qkv_stride, text_qkv, text_token_stride, text_qkv_stride, out_dtype, video_out,
+                             video_token_stride_out, text_sum, ws + l.forward, l.gather - l.forward, stream);
+    if (rc)
+        return rc;
+    unsigned char* gather = ws + l.gather;
+    const size_t slot = (size_t)s.slot_rows * row;  // elements
+    rc = awa_gather_video_shard(plan, heads, head_dim, w0, w1, out_dtype, video_out, video_token_stride_out,
+                                gather + r * slot * osz, stream);
+    if (rc)
+        return rc;
+    rc = nccl_status(n, n->group_start(), "ncclGroupStart");
+    if (rc == AWA_OK)
+        rc = nccl_status(n, n->all_reduce(text_sum, text_sum, (size_t)info.text_tokens * row, ncclFloat32, ncclSum,
+                                          comm->comm, st),
+                         "ncclAllReduce (text partial sums)");
+    if (rc == AWA_OK && slot > 0)
+        rc = nccl_status(n, n->all_gather(gather + r * slot * osz, gather, slot, otype, comm->comm, st),
+                         "ncclAllGather (video rows)");
+    const int end_rc = nccl_status(n, n->group_end(), "ncclGroupEnd");
+    rc = rc ? rc : end_rc;
+    if (rc)
+        return rc;
+    rc = awa_text_finalize(plan, heads, head_dim, text_sum, out_dtype, text_out, text_token_stride_out, stream);
+    for (int q = 0; q < R && rc == AWA_OK; q++)
+        if (q != r)
+            rc = awa_scatter_video_shard(plan, heads, head_dim, s.bounds[q], s.bounds[q + 1], out_dtype,
+                                         gather + q * slot * osz, video_out, video_token_stride_out, stream);
+    return rc;
+}
+
+}  // extern "C"

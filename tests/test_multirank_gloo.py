@@ -1,14 +1,16 @@
-"""Two-rank (gloo, CPU) test of the window-parallel multi-GPU protocol.
+"""Two-rank (gloo, CPU) test of the multi-GPU protocol of awa_forward_sharded.
 
-On GPUs, rank r computes windows [bounds[r], bounds[r+1]) of
-awa_partition_windows with awa_forward_windows (its video rows + an
-unnormalised fp32 text partial sum), the ranks all-reduce the partial and
-call awa_text_finalize (divide by the window count). Here each rank runs the
+On GPUs the split comes from awa_shard_split. With enough windows, rank r
+computes windows [bounds[r], bounds[r+1)) (awa_forward_windows: its video rows
++ an unnormalised fp32 text partial sum), the ranks all-reduce the partial,
+divide by the window count and all-gather the video rows. With fewer than 4
+windows per rank, rank r computes every window for heads [bounds[r],
+bounds[r+1)) and the ranks all-gather the head slices. Here each rank runs the
 same protocol on the CPU with the oracle standing in for the kernels: the
-window split comes from the library's host-side plan, the exchange is a real
-gloo all-reduce / all-gather between two processes, and the result must equal
-the single-process reference chain (video rows bit-exact, text within the
-fp32 tolerance: the cross-rank sum adds in a different order).
+split comes from the library's host-side plan, the exchange is a real gloo
+all-reduce / all-gather between two processes, and the result must equal the
+single-process reference chain (video rows bit-exact, text within the fp32
+tolerance: the cross-rank sum adds in a different order).
 """
 
 from __future__ import annotations
@@ -25,6 +27,8 @@ CASES = [
     # grid, window counts, shifted, heads, head_dim, text tokens
     ((2, 45, 80), (1, 3, 4), True, 2, 16, 6),
     ((3, 12, 20), (2, 3, 4), False, 2, 32, 5),
+    # 3 windows on 2 ranks: split by heads
+    ((1, 12, 20), (1, 1, 3), False, 5, 12, 4),
 ]
 
 
@@ -66,10 +70,10 @@ def _rank_main(rank: int, world: int, port: int, case, result_dir: str):
         h, d, text = cfg.heads, cfg.head_dim, cfg.text_tokens
         plan = awa_b200.AwaPlan(*cfg.params[:6], text_tokens=text, shifted=bool(cfg.shifted), rope_dim=cfg.rope_dim,
                                 host_only=True)
-        bounds = plan.partition(world)
+        by_heads, bounds = plan.shard_split(world, h)
+        assert by_heads == (plan.info.window_count < 4 * world)
         begin, end = bounds[rank], bounds[rank + 1]
         W = plan.info.window_count
-        # this rank's windows, as awa_forward_windows computes them
         maps = oracle.index_maps(cfg)
         seq = maps["sequence_index"]
         cu = maps["cu_seqlens"].astype(np.int32)
@@ -77,31 +81,46 @@ def _rank_main(rank: int, world: int, port: int, case, result_dir: str):
         is_text = seq >= cfg.source_tokens
         packed[is_text] = t[seq[is_text] - cfg.source_tokens]
         roped = oracle.rope(packed, oracle.rope_table(cfg), h, d, cfg.rope_dim)
-        attended = np.zeros((len(seq), h, d), np.float32)
-        if end > begin:
-            oracle.attention_range(roped, cu, begin, end, h, d, attended)
         video = np.zeros((cfg.source_tokens, h, d), np.float32)
-        owned = np.zeros(cfg.source_tokens, np.int32)
+        owned = np.zeros((cfg.source_tokens, h), np.int32)
+        if by_heads:
+            # every window, heads [begin, end): the same math on a head slice
+            hn = end - begin
+            sub = np.ascontiguousarray(roped[:, :, begin:end])
+            att = np.zeros((len(seq), hn, d), np.float32)
+            if hn:
+                oracle.attention_range(sub, cu, 0, W, hn, d, att)
+            attended = np.zeros((len(seq), h, d), np.float32)
+            attended[:, begin:end] = att
+            windows = range(W)
+        else:
+            attended = np.zeros((len(seq), h, d), np.float32)
+            if end > begin:
+                oracle.attention_range(roped, cu, begin, end, h, d, attended)
+            windows = range(begin, end)
+        heads_owned = slice(begin, end) if by_heads else slice(0, h)
         partial = np.zeros((text, h, d), np.float32)
-        for w in range(begin, end):
+        for w in windows:
             rows = np.arange(cu[w], cu[w + 1] - text)
             video[seq[rows]] = attended[rows]
-            owned[seq[rows]] += 1
+            owned[seq[rows], heads_owned] += 1
             partial += attended[cu[w + 1] - text:cu[w + 1]]  # window order, fp32
-        assert int(owned.sum()) == plan.range_video_rows(begin, end)
-        # the exchange: all-reduce of the partials, all-gather of the video rows
+        if not by_heads:
+            assert int(owned[:, 0].sum()) == plan.range_video_rows(begin, end)
+        # the exchange: all-reduce of the partials (a head split's are disjoint),
+        # all-gather of the video rows
         total = torch.from_numpy(partial)
         dist.all_reduce(total, op=dist.ReduceOp.SUM)
         text_out = (total / np.float32(W)).numpy()
         gathered = [torch.zeros(cfg.source_tokens, h, d) for _ in range(world)]
-        owners = [torch.zeros(cfg.source_tokens, dtype=torch.int32) for _ in range(world)]
+        owners = [torch.zeros(cfg.source_tokens, h, dtype=torch.int32) for _ in range(world)]
         dist.all_gather(gathered, torch.from_numpy(video))
         dist.all_gather(owners, torch.from_numpy(owned))
         if rank == 0:
             count = sum(o.numpy() for o in owners)
             merged = sum(g.numpy() for g in gathered)
             np.savez(os.path.join(result_dir, "result.npz"), video=merged, text=text_out, count=count,
-                     bounds=np.array(bounds))
+                     bounds=np.array(bounds), by_heads=by_heads)
     finally:
         dist.destroy_process_group()
 
@@ -117,7 +136,8 @@ def test_window_sharded_protocol_matches_single_process(case, tmp_path, oracle):
     v, t = _inputs(cfg)
     ref = oracle.chain(cfg, v, t)
     bounds = res["bounds"]
-    assert bounds[0] == 0 and bounds[-1] == len(ref["maps"]["windows"]) and np.all(np.diff(bounds) > 0)
-    assert np.all(res["count"] == 1), "every video token must be computed by exactly one rank"
+    last = cfg.heads if bool(res["by_heads"]) else len(ref["maps"]["windows"])
+    assert bounds[0] == 0 and bounds[-1] == last and np.all(np.diff(bounds) > 0)
+    assert np.all(res["count"] == 1), "every video token and head must be computed by exactly one rank"
     assert np.array_equal(res["video"], ref["video"])
     assert rel_l2(res["text"], ref["text"]) <= FP32_REL_L2
