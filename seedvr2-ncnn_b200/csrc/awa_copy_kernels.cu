@@ -9,6 +9,8 @@
 #include "awa_device.cuh"
 #include "awa_internal.h"
 
+#include <algorithm>
+
 #include <cuda_bf16.h>
 
 namespace awa
@@ -368,31 +370,34 @@ __global__ void text_scale(int rows, int head_row, const float* __restrict__ sum
 }
 
 // Video rows of windows [begin, end) between source order and the dense
-// shard order (window by window, video rows only). One block per window.
-template <typename T>
-__global__ void shard_copy_kernel(PlanDevice plan, int head_row, int window_begin, const T* __restrict__ src,
-                                  int64_t src_stride, T* __restrict__ dst, int64_t dst_stride, int to_source)
+// shard order (window by window, video rows only). A warp moves one token row
+// (row_bytes) at a time; blockIdx.y is the window, blockIdx.x a run of
+// kShardRowsPerBlock of its rows. V is the copy word: 16 bytes when row bytes,
+// strides and bases are all 16-byte aligned, else 4 or 2 bytes.
+constexpr int kShardRowsPerBlock = 8;
+
+template <typename V>
+__global__ void __launch_bounds__(32 * kShardRowsPerBlock)
+    shard_copy_kernel(PlanDevice plan, int window_begin, int launch_begin, int row_words, const V* __restrict__ src,
+                      int64_t src_stride_words, V* __restrict__ dst, int64_t dst_stride_words, int to_source)
 {
-    const int w = window_begin + blockIdx.x;
+    const int w = launch_begin + blockIdx.y;
     const WindowDesc win = plan.windows[w];
-    const int64_t shard_base = (int64_t)(plan.cu_seqlens[w] - plan.cu_seqlens[window_begin]) -
-                               (int64_t)(w - window_begin) * plan.text_tokens;
+    const int r = blockIdx.x * kShardRowsPerBlock + (threadIdx.x >> 5);
+    if (r >= win.video)
+        return;
+    const int64_t shard_row = (int64_t)(plan.cu_seqlens[w] - plan.cu_seqlens[window_begin]) -
+                              (int64_t)(w - window_begin) * plan.text_tokens + r;
     const int plane = win.nh * win.nw;
-    const int64_t total = (int64_t)win.video * head_row;
-    for (int64_t id = threadIdx.x; id < total; id += blockDim.x)
-    {
-        const int r = (int)(id / head_row);
-        const int e = (int)(id - (int64_t)r * head_row);
-        const int t = win.t0 + r / plane;
-        const int h = win.h0 + (r % plane) / win.nw;
-        const int x = win.w0 + r % win.nw;
-        const int64_t token = ((int64_t)t * plan.source_h + h) * plan.source_w + x;
-        const int64_t shard_row = shard_base + r;
-        if (to_source)
-            dst[token * dst_stride + e] = src[shard_row * src_stride + e];
-        else
-            dst[shard_row * dst_stride + e] = src[token * src_stride + e];
-    }
+    const int t = win.t0 + r / plane;
+    const int rem = r - (r / plane) * plane;
+    const int h = win.h0 + rem / win.nw;
+    const int x = win.w0 + rem % win.nw;
+    const int64_t token = ((int64_t)t * plan.source_h + h) * plan.source_w + x;
+    const V* from = src + (to_source ? shard_row * src_stride_words : token * src_stride_words);
+    V* to = dst + (to_source ? token * dst_stride_words : shard_row * dst_stride_words);
+    for (int i = threadIdx.x & 31; i < row_words; i += 32)
+        to[i] = from[i];
 }
 
 template <template <typename, typename> class Fn, typename... Args>
@@ -607,14 +612,38 @@ int launch_shard_copy(const PlanDevice& plan, int heads, int head_dim, int windo
                       cudaStream_t stream)
 {
     ProfileScope prof("awa_shard_copy", stream);
-    const int head_row = heads * head_dim;
-    const int blocks = window_end - window_begin;
-    if (dtype == kF32)
-        shard_copy_kernel<float><<<blocks, 256, 0, stream>>>(plan, head_row, window_begin, (const float*)src, src_stride,
-                                                             (float*)dst, dst_stride, to_source);
-    else
-        shard_copy_kernel<bf16><<<blocks, 256, 0, stream>>>(plan, head_row, window_begin, (const bf16*)src, src_stride,
-                                                            (bf16*)dst, dst_stride, to_source);
+    const int64_t esize = dtype == kF32 ? 4 : 2;
+    const int64_t row_bytes = (int64_t)heads * head_dim * esize;
+    const int64_t sb = src_stride * esize, db = dst_stride * esize;
+    // blockIdx.y is the window (at most 65535 per launch), blockIdx.x runs over
+    // the longest window's video rows
+    if (window_end <= window_begin)
+        return 0;
+    if (plan.max_window_video <= 0)
+        return (int)cudaErrorInvalidValue;
+    const int max_rows = plan.max_window_video;
+    const dim3 block(32 * kShardRowsPerBlock);
+    const uintptr_t bases = reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst);
+    const bool v16 = row_bytes % 16 == 0 && sb % 16 == 0 && db % 16 == 0 && bases % 16 == 0;
+    const bool v4 = row_bytes % 4 == 0 && sb % 4 == 0 && db % 4 == 0 && bases % 4 == 0;
+    for (int w0 = window_begin; w0 < window_end; w0 += 65535)
+    {
+        // windows [w0, w1): shard rows of this launch start where window w0's do
+        const int w1 = std::min(window_end, w0 + 65535);
+        const dim3 grid((unsigned)((max_rows + kShardRowsPerBlock - 1) / kShardRowsPerBlock), (unsigned)(w1 - w0));
+        if (v16)
+            shard_copy_kernel<uint4><<<grid, block, 0, stream>>>(plan, window_begin, w0, (int)(row_bytes / 16),
+                                                                 (const uint4*)src, sb / 16, (uint4*)dst, db / 16,
+                                                                 to_source);
+        else if (v4)
+            shard_copy_kernel<uint32_t><<<grid, block, 0, stream>>>(plan, window_begin, w0, (int)(row_bytes / 4),
+                                                                    (const uint32_t*)src, sb / 4, (uint32_t*)dst,
+                                                                    db / 4, to_source);
+        else
+            shard_copy_kernel<unsigned short><<<grid, block, 0, stream>>>(
+                plan, window_begin, w0, (int)(row_bytes / 2), (const unsigned short*)src, sb / 2,
+                (unsigned short*)dst, db / 2, to_source);
+    }
     return (int)cudaGetLastError();
 }
 

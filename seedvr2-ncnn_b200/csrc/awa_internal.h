@@ -41,6 +41,7 @@ struct PlanDevice
     int rope_dim = 0;
     int pairs_per_axis = 0;  // rope_dim / 6
     int max_coord = 0;
+    int max_window_video = 0;  // most video rows of one window
     // Slab geometry of the tcgen05 kernel's fused path. A window's video rows
     // are fetched as boxes of tc_bhc x tc_bwc (h x w) tokens of one frame,
     // laid over the nominal window (tc_bh x tc_bw from (h0n, w0n)); every box

@@ -516,6 +516,7 @@ static int plan_create_impl(const awa_layer_params* params, const awa_runtime_sp
     dev.rope_dim = rope_dim;
     dev.pairs_per_axis = plan->pairs_per_axis;
     dev.max_coord = max_coord;
+    dev.max_window_video = max_length - text;
     if (!awa::device_error_flag())
     {
         cudaFree(plan->device_block);

@@ -33,7 +33,8 @@ CASES = [
     ("cfg2-windows", LayerConfig(6, 16, 16, 2, 8, 8, shifted=0), BF16, True),
     ("cfg2-shifted-windows", LayerConfig(6, 16, 16, 2, 8, 8, shifted=1), BF16, True),
     ("cfg1-heads-bf16", LayerConfig(1, 16, 16, 1, 8, 8, shifted=0), BF16, True),
-    ("cfg1-heads-fp32", LayerConfig(1, 16, 16, 1, 8, 8, shifted=1), FP32, True),
+    ("cfg1-heads-fp32", LayerConfig(1, 16, 16, 1, 8, 8, shifted=0), FP32, True),
+    ("cfg1-shifted-fp32", LayerConfig(1, 16, 16, 1, 8, 8, shifted=1), FP32, True),
     ("cfg5-fp32-shifted", LayerConfig(9, 45, 80, 3, 6, 10, shifted=1), FP32, False),
     ("cfg4", LayerConfig(21, 64, 64, 6, 8, 8, shifted=0), BF16, False),
 ]

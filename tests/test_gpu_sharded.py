@@ -55,7 +55,8 @@ def rank_results(tmp_path_factory):
     return [json.load(open(out / f"rank{r}.json")) for r in range(WORLD)]
 
 
-CASES = ["cfg2-windows", "cfg2-shifted-windows", "cfg1-heads-bf16", "cfg1-heads-fp32", "cfg5-fp32-shifted", "cfg4"]
+CASES = ["cfg2-windows", "cfg2-shifted-windows", "cfg1-heads-bf16", "cfg1-heads-fp32", "cfg1-shifted-fp32",
+         "cfg5-fp32-shifted", "cfg4"]
 
 
 @pytest.mark.parametrize("name", CASES)
