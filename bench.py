@@ -303,7 +303,12 @@ def run_sharded(args, rank, world, local_rank):
     gen = torch.Generator(device=device).manual_seed(1234)  # the same layer on every rank
     video_qkv = torch.randn(n_v, 3, HEADS, HEAD_DIM, device=device, generator=gen).to(dtype)
     text_qkv = torch.randn(TEXT, 3, HEADS, HEAD_DIM, device=device, generator=gen).to(dtype)
-    video_out = torch.empty(n_v, HEADS, HEAD_DIM, device=device, dtype=dtype)
+    direct = args.exchange == "p2p"
+    # p2p: the video output lives in a buffer shared over the ranks, and the
+    # attention kernel stores each row into every rank's copy over NVLink;
+    # nccl: each rank keeps its own output and NCCL all-gathers the rows
+    video_out = (comm.shared_tensor((n_v, HEADS, HEAD_DIM), dtype) if direct else
+                 torch.empty(n_v, HEADS, HEAD_DIM, device=device, dtype=dtype))
     text_out = torch.empty(TEXT, HEADS, HEAD_DIM, device=device, dtype=dtype)
     workspace = torch.empty(plan.sharded_workspace_bytes(world, HEADS, HEAD_DIM, dtype), device=device,
                             dtype=torch.uint8)
@@ -390,6 +395,8 @@ def run_sharded(args, rank, world, local_rank):
         e2e_ms = float(te.item()) / e2e_steps
     clock = clocks.stop()
     awa_b200.device_status()
+    if direct:
+        comm.free_shared(video_out)
     comm.destroy()
 
     hbm_peak, tensor_peak, peak_src = measured_peaks()
@@ -410,6 +417,9 @@ def run_sharded(args, rank, world, local_rank):
             "config": workload_config(name, world, "sharded"),
             "windows": W, "attn_tflops": round(flops / (ms_per_step / 1000.0) / 1e12, 2),
             "sharded": {"split": "heads" if by_heads else "windows", "bounds": bounds,
+                        "exchange": ("video rows stored by the attention kernel into every rank's output over NVLink "
+                                     "(P2P); NCCL all-reduce of the text partial sums" if direct else
+                                     "NCCL all-gather of the video rows, all-reduce of the text partial sums"),
                         "compute_ms_max": round(compute_ms_max, 5),
                         "collective_and_copies_ms": round(ms_per_step - compute_ms_max, 5),
                         "kernel_only_value": round(W / (compute_ms_max / 1000.0), 2)},
@@ -978,6 +988,9 @@ def main():
     parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
     parser.add_argument("--workload", default="cfg4", choices=sorted(WORKLOADS))
     parser.add_argument("--e2e-steps", type=int, default=20)
+    parser.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                        help="sharded mode: p2p = the attention kernel stores video rows into every rank's output "
+                             "(shared buffer); nccl = NCCL all-gather of the rows")
     parser.add_argument("--mode", default=None, choices=["sharded", "replicas"],
                         help="N > 1: sharded (default) splits one layer over the N GPUs with NCCL (strong scaling); "
                              "replicas runs an independent layer per GPU (weak scaling)")

@@ -247,7 +247,19 @@ int awa_comm_unique_id(unsigned char* id, size_t capacity);
 int awa_comm_create(const unsigned char* id, size_t id_bytes, int nranks, int rank, awa_comm** out);
 /* Uses the caller's own ncclComm_t (not destroyed by awa_comm_destroy). */
 int awa_comm_wrap(void* nccl_comm, awa_comm** out);
+/* Frees any shared buffer still held (without the barrier of
+ * awa_comm_free_shared) and the communicator. */
 void awa_comm_destroy(awa_comm* comm);
+/* Collective: a device buffer of `bytes` on every rank, each mapped into every
+ * other rank's address space (CUDA IPC over NVLink). When video_out of
+ * awa_forward_sharded lies in such a buffer and the tensor-core kernel runs,
+ * the kernel stores each video row straight into every rank's copy (P2P stores
+ * overlapping the attention; no all-gather, staging or scatter of the video
+ * rows), behind an entry barrier so no rank overwrites rows another still
+ * reads. *ptr is the local buffer (zeroed). */
+int awa_comm_alloc_shared(awa_comm* comm, size_t bytes, void** ptr);
+/* Collective: waits for every rank, unmaps and frees a shared buffer. */
+int awa_comm_free_shared(awa_comm* comm, void* ptr);
 int awa_comm_info(const awa_comm* comm, int* rank, int* nranks);
 /* The split awa_forward_sharded uses for nranks ranks: *by_heads (0/1) and
  * nranks+1 bounds (window indices, or head indices for a head split). */

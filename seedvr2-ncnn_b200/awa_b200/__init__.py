@@ -42,6 +42,7 @@ EXPORTED_SYMBOLS = (
     "awa_window_range_video_rows", "awa_partition_windows", "awa_qkv_project", "awa_out_project", "awa_device_status",
     "awa_selftest_bounded_wait", "awa_attention_kernel_kind",
     "awa_comm_unique_id", "awa_comm_create", "awa_comm_wrap", "awa_comm_destroy", "awa_comm_info", "awa_shard_split",
+    "awa_comm_alloc_shared", "awa_comm_free_shared",
     "awa_forward_sharded_workspace_bytes", "awa_forward_sharded",
     "awa_profile_enable", "awa_profile_reset", "awa_profile_collect", "awa_last_error", "awa_version",
     "awa_graph_find_chains", "awa_graph_find_chains_file", "awa_graph_make_dynamic", "awa_manifest_validate",
@@ -137,6 +138,8 @@ def library() -> ctypes.CDLL:
         "awa_comm_create": (i, [p, sz, i, i, ctypes.POINTER(p)]),
         "awa_comm_wrap": (i, [p, ctypes.POINTER(p)]),
         "awa_comm_destroy": (None, [p]),
+        "awa_comm_alloc_shared": (i, [p, sz, ctypes.POINTER(p)]),
+        "awa_comm_free_shared": (i, [p, p]),
         "awa_comm_info": (i, [p, ctypes.POINTER(i), ctypes.POINTER(i)]),
         "awa_shard_split": (i, [p, i, i, ctypes.POINTER(i), p]),
         "awa_forward_sharded_workspace_bytes": (sz, [p, i, i, i, i]),
@@ -598,6 +601,35 @@ class AwaComm:
     @property
     def handle(self):
         return self._handle
+
+    def shared_tensor(self, shape, dtype):
+        """Collective: a torch tensor over a buffer shared by every rank
+        (awa_comm_alloc_shared). A video output in such a buffer lets
+        forward_sharded store rows straight into every rank's copy. Release
+        with free_shared (collective)."""
+        torch = _torch()
+        import math as _math
+
+        nbytes = _math.prod(shape) * torch.tensor([], dtype=dtype).element_size()
+        ptr = ctypes.c_void_p()
+        _check(library().awa_comm_alloc_shared(self._handle, nbytes, ctypes.byref(ptr)))
+        typestr = {torch.bfloat16: "<i2", torch.float32: "<f4"}[dtype]
+
+        class _Iface:
+            __cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr.value, False),
+                                        "version": 3, "strides": None}
+
+        t = torch.as_tensor(_Iface(), device="cuda")
+        if dtype == torch.bfloat16:
+            t = t.view(torch.bfloat16)
+        self._shared = getattr(self, "_shared", [])
+        self._shared.append(ptr.value)
+        return t
+
+    def free_shared(self, tensor) -> None:
+        ptr = tensor.data_ptr()
+        _check(library().awa_comm_free_shared(self._handle, ctypes.c_void_p(ptr)))
+        self._shared = [p for p in getattr(self, "_shared", []) if p != ptr]
 
     def destroy(self) -> None:
         if getattr(self, "_handle", None) and _lib is not None:

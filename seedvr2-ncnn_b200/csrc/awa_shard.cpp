@@ -118,6 +118,15 @@ size_t dsize(int dtype)
 
 }  // namespace
 
+// A device buffer of every rank mapped into every rank's address space (CUDA
+// IPC): peer[q] is rank q's buffer (peer[rank] the local one).
+struct SharedBuffer
+{
+    void* local = nullptr;
+    size_t bytes = 0;
+    std::vector<void*> peer;
+};
+
 struct awa_comm
 {
     ncclComm_t comm = nullptr;
@@ -125,6 +134,8 @@ struct awa_comm
     int nranks = 1;
     int device = -1;
     bool owned = false;
+    std::vector<SharedBuffer> shared;
+    int* barrier_word = nullptr;  // device int for the entry barrier of the direct mode
 };
 
 namespace
@@ -196,9 +207,126 @@ Layout make_layout(const awa_plan* plan, const awa_plan_info& info, const Split&
     return l;
 }
 
+// The shared buffer that holds [p, p + bytes) on this rank, or nullptr.
+const SharedBuffer* find_shared(const awa_comm* c, const void* p, size_t bytes)
+{
+    const unsigned char* q = static_cast<const unsigned char*>(p);
+    for (const SharedBuffer& b : c->shared)
+    {
+        const unsigned char* base = static_cast<const unsigned char*>(b.local);
+        if (q >= base && q + bytes <= base + b.bytes)
+            return &b;
+    }
+    return nullptr;
+}
+
+void release_shared(SharedBuffer& b, int rank)
+{
+    for (size_t q = 0; q < b.peer.size(); q++)
+        if ((int)q != rank && b.peer[q])
+            cudaIpcCloseMemHandle(b.peer[q]);
+    if (b.local)
+        cudaFree(b.local);
+    b = SharedBuffer();
+}
+
+// All ranks reach this point on `stream` before any goes on (a one-word NCCL
+// all-reduce).
+int barrier(const Nccl* n, awa_comm* c, cudaStream_t stream)
+{
+    return nccl_status(n, n->all_reduce(c->barrier_word, c->barrier_word, 1, ncclInt32, ncclSum, c->comm, stream),
+                       "ncclAllReduce (barrier)");
+}
+
 }  // namespace
 
 extern "C" {
+
+int awa_comm_alloc_shared(awa_comm* comm, size_t bytes, void** out)
+{
+    if (!comm || !out || bytes == 0)
+        return fail(AWA_ERR_INVALID, "awa_comm_alloc_shared: invalid arguments");
+    *out = nullptr;
+    const Nccl* n = nccl();
+    if (!n)
+        return fail(AWA_ERR_CUDA, "awa_comm_alloc_shared: libnccl.so.2 could not be loaded");
+    const int R = comm->nranks;
+    SharedBuffer b;
+    b.bytes = bytes;
+    b.peer.assign(R, nullptr);
+    unsigned char* handles = nullptr;
+    cudaStream_t st = nullptr;
+    cudaError_t e = cudaMalloc(&b.local, bytes);
+    if (e == cudaSuccess)
+        e = cudaMemset(b.local, 0, bytes);
+    cudaIpcMemHandle_t mine;
+    if (e == cudaSuccess)
+        e = cudaIpcGetMemHandle(&mine, b.local);
+    if (e == cudaSuccess)
+        e = cudaMalloc(&handles, (size_t)R * sizeof(cudaIpcMemHandle_t));
+    if (e == cudaSuccess)
+        e = cudaMemcpy(handles + comm->rank * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    int rc = cuda_status(e, "awa_comm_alloc_shared");
+    // every rank's handle to every rank
+    if (rc == AWA_OK)
+        rc = nccl_status(n, n->all_gather(handles + comm->rank * sizeof(mine), handles, sizeof(mine), ncclUint8,
+                                          comm->comm, st),
+                         "ncclAllGather (IPC handles)");
+    std::vector<cudaIpcMemHandle_t> all(R);
+    if (rc == AWA_OK)
+        rc = cuda_status(cudaStreamSynchronize(st), "awa_comm_alloc_shared");
+    if (rc == AWA_OK)
+        rc = cuda_status(cudaMemcpy(all.data(), handles, (size_t)R * sizeof(mine), cudaMemcpyDeviceToHost),
+                         "awa_comm_alloc_shared");
+    for (int q = 0; q < R && rc == AWA_OK; q++)
+    {
+        if (q == comm->rank)
+        {
+            b.peer[q] = b.local;
+            continue;
+        }
+        rc = cuda_status(cudaIpcOpenMemHandle(&b.peer[q], all[q], cudaIpcMemLazyEnablePeerAccess),
+                         "cudaIpcOpenMemHandle");
+    }
+    if (st)
+        cudaStreamDestroy(st);
+    if (handles)
+        cudaFree(handles);
+    if (rc != AWA_OK)
+    {
+        release_shared(b, comm->rank);
+        return rc;
+    }
+    comm->shared.push_back(b);
+    *out = b.local;
+    return AWA_OK;
+}
+
+int awa_comm_free_shared(awa_comm* comm, void* ptr)
+{
+    if (!comm || !ptr)
+        return fail(AWA_ERR_INVALID, "awa_comm_free_shared: invalid arguments");
+    const Nccl* n = nccl();
+    if (!n)
+        return fail(AWA_ERR_CUDA, "awa_comm_free_shared: libnccl.so.2 could not be loaded");
+    for (size_t i = 0; i < comm->shared.size(); i++)
+        if (comm->shared[i].local == ptr)
+        {
+            // no rank may still be writing into another's buffer: finish this
+            // rank's work, then wait for every rank
+            int rc = cuda_status(cudaDeviceSynchronize(), "awa_comm_free_shared");
+            if (rc == AWA_OK)
+                rc = barrier(n, comm, nullptr);
+            if (rc == AWA_OK)
+                rc = cuda_status(cudaDeviceSynchronize(), "awa_comm_free_shared");
+            release_shared(comm->shared[i], comm->rank);
+            comm->shared.erase(comm->shared.begin() + i);
+            return rc;
+        }
+    return fail(AWA_ERR_INVALID, "awa_comm_free_shared: not a buffer of this communicator");
+}
 
 int awa_comm_unique_id(unsigned char* id, size_t capacity)
 {
@@ -241,6 +369,13 @@ int awa_comm_create(const unsigned char* id, size_t id_bytes, int nranks, int ra
     c->rank = rank;
     c->nranks = nranks;
     c->owned = true;
+    if (cudaMalloc(&c->barrier_word, sizeof(int)) != cudaSuccess ||
+        cudaMemset(c->barrier_word, 0, sizeof(int)) != cudaSuccess)
+    {
+        n->comm_destroy(c->comm);
+        delete c;
+        return fail(AWA_ERR_ALLOC, "awa_comm_create: device allocation failed");
+    }
     *out = c;
     return AWA_OK;
 }
@@ -260,6 +395,9 @@ int awa_comm_wrap(void* nccl_comm, awa_comm** out)
         rc = nccl_status(n, n->comm_user_rank(c->comm, &c->rank), "ncclCommUserRank");
     if (rc == AWA_OK && cudaGetDevice(&c->device) != cudaSuccess)
         rc = fail(AWA_ERR_CUDA, "awa_comm_wrap: no current device");
+    if (rc == AWA_OK && (cudaMalloc(&c->barrier_word, sizeof(int)) != cudaSuccess ||
+                         cudaMemset(c->barrier_word, 0, sizeof(int)) != cudaSuccess))
+        rc = fail(AWA_ERR_ALLOC, "awa_comm_wrap: device allocation failed");
     if (rc != AWA_OK)
     {
         delete c;
@@ -273,6 +411,10 @@ void awa_comm_destroy(awa_comm* comm)
 {
     if (!comm)
         return;
+    for (SharedBuffer& b : comm->shared)
+        release_shared(b, comm->rank);
+    if (comm->barrier_word)
+        cudaFree(comm->barrier_word);
     const Nccl* n = nccl();
     if (comm->owned && comm->comm && n)
         n->comm_destroy(comm->comm);
@@ -343,6 +485,30 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
     const int64_t row = (int64_t)heads * head_dim;
     int rc = AWA_OK;
 
+    // Direct mode: video_out lies in a buffer shared over the ranks and the
+    // tensor-core kernel runs. The kernel then stores each video row into every
+    // rank's copy of video_out as it computes it (P2P stores over NVLink), so
+    // the video rows need no all-gather, staging or scatter. An entry barrier
+    // keeps any rank from writing before every rank has finished with the
+    // previous contents; the text collective at the end orders the stores
+    // before every rank's later reads.
+    const size_t video_span = (size_t)(info.source_tokens - 1) * video_token_stride_out * osz + (size_t)row * osz;
+    const SharedBuffer* shared = find_shared(comm, video_out, video_span);
+    const int head_hint = s.by_heads ? s.bounds[1] - s.bounds[0] : heads;
+    const bool direct = shared && R - 1 <= awa::AttnArgs::kMaxPeers &&
+                        awa_attention_kernel_kind(plan, precision, in_dtype, std::max(head_hint, 1), head_dim) == 1;
+    std::vector<void*> peers;
+    if (direct)
+    {
+        const size_t off = static_cast<unsigned char*>(video_out) - static_cast<unsigned char*>(shared->local);
+        for (int q = 0; q < R; q++)
+            if (q != r)
+                peers.push_back(static_cast<unsigned char*>(shared->peer[q]) + off);
+        rc = barrier(n, comm, st);
+        if (rc)
+            return rc;
+    }
+
     if (s.by_heads)
     {
         // This rank's heads [h0, h1) over every window: offset pointers, same strides.
@@ -351,14 +517,18 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
         for (int q = 0; q < R; q++)
             most = std::max(most, s.bounds[q + 1] - s.bounds[q]);
         const size_t hoff_in = (size_t)h0 * head_dim * isz, hoff_out = (size_t)h0 * head_dim * osz;
+        std::vector<void*> head_peers;
+        for (void* p : peers)
+            head_peers.push_back(static_cast<unsigned char*>(p) + hoff_out);
         if (hn > 0)
-            rc = awa_forward(plan, precision, hn, head_dim, in_dtype,
-                             static_cast<const unsigned char*>(video_qkv) + hoff_in, video_token_stride,
-                             video_qkv_stride, static_cast<const unsigned char*>(text_qkv) + hoff_in,
-                             text_token_stride, text_qkv_stride, out_dtype,
-                             static_cast<unsigned char*>(video_out) + hoff_out, video_token_stride_out,
-                             static_cast<unsigned char*>(text_out) + hoff_out, text_token_stride_out,
-                             ws + l.forward, l.gather - l.forward, stream);
+            rc = awa::forward_to_peers(plan, precision, hn, head_dim, in_dtype,
+                                       static_cast<const unsigned char*>(video_qkv) + hoff_in, video_token_stride,
+                                       video_qkv_stride, static_cast<const unsigned char*>(text_qkv) + hoff_in,
+                                       text_token_stride, text_qkv_stride, out_dtype,
+                                       static_cast<unsigned char*>(video_out) + hoff_out, video_token_stride_out,
+                                       static_cast<unsigned char*>(text_out) + hoff_out, text_token_stride_out,
+                                       ws + l.forward, l.gather - l.forward, head_peers.data(),
+                                       (int)head_peers.size(), st);
         if (rc)
             return rc;
         // Pack this rank's head slices into its slots ([N_v][most][d] and [T][most][d]).
@@ -366,24 +536,24 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
         unsigned char* vg = ws + l.gather;
         unsigned char* tg = ws + l.text_gather;
         const size_t width = (size_t)hn * head_dim * osz, spitch = (size_t)most * head_dim * osz;
-        if (hn > 0)
+        if (hn > 0 && !direct)
         {
             rc = cuda_status(cudaMemcpy2DAsync(vg + r * vslot * osz, spitch,
                                                static_cast<unsigned char*>(video_out) + hoff_out,
                                                video_token_stride_out * osz, width, info.source_tokens,
                                                cudaMemcpyDeviceToDevice, st),
                              "head slice pack (video)");
-            if (rc == AWA_OK)
-                rc = cuda_status(cudaMemcpy2DAsync(tg + r * tslot * osz, spitch,
-                                                   static_cast<unsigned char*>(text_out) + hoff_out,
-                                                   text_token_stride_out * osz, width, info.text_tokens,
-                                                   cudaMemcpyDeviceToDevice, st),
-                                 "head slice pack (text)");
         }
+        if (hn > 0 && rc == AWA_OK)
+            rc = cuda_status(cudaMemcpy2DAsync(tg + r * tslot * osz, spitch,
+                                               static_cast<unsigned char*>(text_out) + hoff_out,
+                                               text_token_stride_out * osz, width, info.text_tokens,
+                                               cudaMemcpyDeviceToDevice, st),
+                             "head slice pack (text)");
         if (rc)
             return rc;
         rc = nccl_status(n, n->group_start(), "ncclGroupStart");
-        if (rc == AWA_OK)
+        if (rc == AWA_OK && !direct)
             rc = nccl_status(n, n->all_gather(vg + r * vslot * osz, vg, vslot, otype, comm->comm, st), "ncclAllGather (video)");
         if (rc == AWA_OK)
             rc = nccl_status(n, n->all_gather(tg + r * tslot * osz, tg, tslot, otype, comm->comm, st), "ncclAllGather (text)");
@@ -397,10 +567,11 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
             if (q == r || qn == 0)
                 continue;
             const size_t qoff = (size_t)s.bounds[q] * head_dim * osz, qwidth = (size_t)qn * head_dim * osz;
-            rc = cuda_status(cudaMemcpy2DAsync(static_cast<unsigned char*>(video_out) + qoff,
-                                               video_token_stride_out * osz, vg + q * vslot * osz, spitch, qwidth,
-                                               info.source_tokens, cudaMemcpyDeviceToDevice, st),
-                             "head slice unpack (video)");
+            if (!direct)
+                rc = cuda_status(cudaMemcpy2DAsync(static_cast<unsigned char*>(video_out) + qoff,
+                                                   video_token_stride_out * osz, vg + q * vslot * osz, spitch, qwidth,
+                                                   info.source_tokens, cudaMemcpyDeviceToDevice, st),
+                                 "head slice unpack (video)");
             if (rc == AWA_OK)
                 rc = cuda_status(cudaMemcpy2DAsync(static_cast<unsigned char*>(text_out) + qoff,
                                                    text_token_stride_out * osz, tg + q * tslot * osz, spitch, qwidth,
@@ -413,11 +584,21 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
     // Window split: this rank's windows [w0, w1).
     const int w0 = s.bounds[r], w1 = s.bounds[r + 1];
     float* text_sum = reinterpret_cast<float*>(ws + l.text_sum);
-    rc = awa_forward_windows(plan, precision, heads, head_dim, w0, w1, in_dtype, video_qkv, video_token_stride,
-                             video_qkv_stride, text_qkv, text_token_stride, text_qkv_stride, out_dtype, video_out,
-                             video_token_stride_out, text_sum, ws + l.forward, l.gather - l.forward, stream);
+    rc = awa::forward_windows_to_peers(plan, precision, heads, head_dim, w0, w1, in_dtype, video_qkv,
+                                       video_token_stride, video_qkv_stride, text_qkv, text_token_stride,
+                                       text_qkv_stride, out_dtype, video_out, video_token_stride_out, text_sum,
+                                       ws + l.forward, l.gather - l.forward, peers.data(), (int)peers.size(), st);
     if (rc)
         return rc;
+    if (direct)
+    {
+        rc = nccl_status(n, n->all_reduce(text_sum, text_sum, (size_t)info.text_tokens * row, ncclFloat32, ncclSum,
+                                          comm->comm, st),
+                         "ncclAllReduce (text partial sums)");
+        if (rc)
+            return rc;
+        return awa_text_finalize(plan, heads, head_dim, text_sum, out_dtype, text_out, text_token_stride_out, stream);
+    }
     unsigned char* gather = ws + l.gather;
     const size_t slot = (size_t)s.slot_rows * row;  // elements
     rc = awa_gather_video_shard(plan, heads, head_dim, w0, w1, out_dtype, video_out, video_token_stride_out,

@@ -65,6 +65,16 @@ def main(rank: int, world: int, port: int, out_path: str) -> None:
         video_s, text_s = plan.forward_sharded(comm, v, t, prec, out_dtype=torch.float32)
         video_b, text_b = plan.forward_sharded(comm, v, t, prec, out_dtype=dtype)  # outputs in the block dtype
         video_1, text_1 = plan.forward(v, t, prec, out_dtype=torch.float32)
+        # direct mode: the video output in a buffer shared over the ranks, rows
+        # stored straight into every rank's copy by the tensor-core kernel
+        shared = comm.shared_tensor((cfg.source_tokens, cfg.heads, cfg.head_dim), torch.float32)
+        shared.fill_(float("nan"))
+        torch.cuda.synchronize()
+        video_d, text_d = plan.forward_sharded(comm, v, t, prec, out_dtype=torch.float32, video_out=shared)
+        torch.cuda.synchronize()
+        direct_equal = bool(torch.equal(video_d, video_1))
+        direct_text_rel = rel_l2(text_d.cpu().numpy(), text_1.cpu().numpy())
+        comm.free_shared(shared)
         torch.cuda.synchronize()
         status = 0
         try:
@@ -74,6 +84,7 @@ def main(rank: int, world: int, port: int, out_path: str) -> None:
         res = {
             "by_heads": by_heads, "bounds": bounds, "status": status,
             "video_equal": bool(torch.equal(video_s, video_1)),
+            "direct_video_equal": direct_equal, "direct_text_rel": direct_text_rel,
             "text_rel": rel_l2(text_s.cpu().numpy(), text_1.cpu().numpy()),
             "video_block_rel": rel_l2(video_b.float().cpu().numpy(), video_1.cpu().numpy()),
             "text_block_rel": rel_l2(text_b.float().cpu().numpy(), text_1.cpu().numpy()),

@@ -8,7 +8,10 @@ grouping (per-rank partial sums, then the all-reduce), so it agrees to fp32
 rounding. Small layers are also checked against the oracle's whole chain.
 Covered: the window split (cfg2, cfg2 shifted, cfg4, cfg5-fp32 shifted) and
 the head split of a layer with fewer than 4 windows per rank (cfg1, 4 windows),
-bf16 (tensor cores) and fp32 (SIMT), fp32 and block-dtype outputs.
+bf16 (tensor cores) and fp32 (SIMT), fp32 and block-dtype outputs, and the
+direct mode, where the video output lies in a buffer shared over the ranks
+(awa_comm_alloc_shared) and the tensor-core kernel stores each row into every
+rank's copy over NVLink.
 """
 
 import json
@@ -68,7 +71,11 @@ def test_sharded_layer_matches_single_gpu(rank_results, name):
         assert r["by_heads"] == ("heads" in name), r
         assert r["video_equal"], (rank, name)
         assert r["text_rel"] < 1e-6, (rank, r["text_rel"])
-        block_tol = 1e-2 if bf16 else 1e-7
+        # the video output in a buffer shared over the ranks (P2P stores from the
+        # tensor-core kernel; the fp32 layers take the all-gather path)
+        assert r["direct_video_equal"], (rank, name, "direct")
+        assert r["direct_text_rel"] < 1e-6, (rank, r["direct_text_rel"])
+        block_tol = 1e-2 if bf16 else 1e-6
         assert r["video_block_rel"] < block_tol and r["text_block_rel"] < block_tol, r
     r0 = rank_results[0][name]
     if "oracle_video_rel" in r0:

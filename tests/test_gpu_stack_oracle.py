@@ -137,6 +137,7 @@ def gpu_step():
                "windows_w": WINDOWS[2], "text_tokens": TEXT, "shifted": b % 2, "rope_dim": 126} for b in range(BLOCKS)]
     stack = awa_b200.AwaStack(params, runtime_spec=GRID, fp32_blocks=FP32_BLOCKS, heads=HEADS, head_dim=HEAD_DIM)
     step = Step()
+    torch.cuda.synchronize()  # weights and inputs were made on the default stream
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
         stack.run(step.hook, stream)
