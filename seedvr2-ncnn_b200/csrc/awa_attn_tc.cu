@@ -1144,12 +1144,9 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
                 // this thread's row: 64 fp32 (fp32 out) or bf16 values (bf16 out, and
                 // the text partials, as the layer chain's bf16 attended rows)
                 const bool f32 = !(!PACKED && text_row) && sizeof(TOut) == 4;
-                const int64_t out_byte = (dst + h * 64) * (int64_t)sizeof(TOut);
                 char* row = (!PACKED && text_row)
                                 ? reinterpret_cast<char*>(reinterpret_cast<bf16*>(a.text_partial) + dst + h * 64)
-                                : static_cast<char*>(a.out) + out_byte;
-                // a layer sharded over GPUs: video rows also go to the peers' outputs
-                const int peers = (!PACKED && !text_row) ? a.peer_count : 0;
+                                : static_cast<char*>(a.out) + (dst + h * 64) * (int64_t)sizeof(TOut);
                 if (f32)
                 {
 #pragma unroll
@@ -1160,23 +1157,18 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
                         o[i] = __float_as_uint(a0);
                         o[i + 1] = __float_as_uint(a1);
                     }
-                    for (int p = -1; p < peers; p++)
+                    if (a.out_v8)
                     {
-                        char* to = p < 0 ? row : static_cast<char*>(a.peer_out[p]) + out_byte;
-                        if (a.out_v8)
-                        {
 #pragma unroll
-                            for (int i = 0; i < 8; i++)
-                                st_global_v8(to + 32 * i, o[8 * i], o[8 * i + 1], o[8 * i + 2], o[8 * i + 3],
-                                             o[8 * i + 4], o[8 * i + 5], o[8 * i + 6], o[8 * i + 7]);
-                        }
-                        else
-                        {
+                        for (int i = 0; i < 8; i++)
+                            st_global_v8(row + 32 * i, o[8 * i], o[8 * i + 1], o[8 * i + 2], o[8 * i + 3], o[8 * i + 4],
+                                         o[8 * i + 5], o[8 * i + 6], o[8 * i + 7]);
+                    }
+                    else
+                    {
 #pragma unroll
-                            for (int i = 0; i < 16; i++)
-                                reinterpret_cast<uint4*>(to)[i] =
-                                    make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-                        }
+                        for (int i = 0; i < 16; i++)
+                            reinterpret_cast<uint4*>(row)[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
                     }
                 }
                 else
@@ -1189,23 +1181,19 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
                         mul_x2(a0, a1, __uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]), inv);
                         pk[i] = pack_bf16x2(a0, a1);
                     }
-                    for (int p = -1; p < peers; p++)
+                    if (a.out_v8)
                     {
-                        char* to = p < 0 ? row : static_cast<char*>(a.peer_out[p]) + out_byte;
-                        if (a.out_v8)
-                        {
 #pragma unroll
-                            for (int i = 0; i < 4; i++)
-                                st_global_v8(to + 32 * i, pk[8 * i], pk[8 * i + 1], pk[8 * i + 2], pk[8 * i + 3],
-                                             pk[8 * i + 4], pk[8 * i + 5], pk[8 * i + 6], pk[8 * i + 7]);
-                        }
-                        else
-                        {
+                        for (int i = 0; i < 4; i++)
+                            st_global_v8(row + 32 * i, pk[8 * i], pk[8 * i + 1], pk[8 * i + 2], pk[8 * i + 3],
+                                         pk[8 * i + 4], pk[8 * i + 5], pk[8 * i + 6], pk[8 * i + 7]);
+                    }
+                    else
+                    {
 #pragma unroll
-                            for (int i = 0; i < 8; i++)
-                                reinterpret_cast<uint4*>(to)[i] =
-                                    make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
-                        }
+                        for (int i = 0; i < 8; i++)
+                            reinterpret_cast<uint4*>(row)[i] =
+                                make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
                     }
                 }
             }
@@ -1213,11 +1201,6 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
         tc::fence_before_sync();
         mbar_arrive(&sh.bar.o_empty[slot]);
     }
-    // Rows stored into peers' memory are made visible system-wide before this
-    // thread ends: the collective the host enqueues after the kernel (and that
-    // the peers wait on) then orders them before the peers' reads.
-    if (a.peer_count > 0)
-        __threadfence_system();
 }
 
 template <bool PACKED, typename TOut, int RD>

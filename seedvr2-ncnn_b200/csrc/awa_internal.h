@@ -97,12 +97,6 @@ struct AttnArgs
     int window_begin = 0;  // fused, sharded: first window of this launch
     int* error_flag = nullptr;
     int out_v8 = 0;  // tcgen05 kernel: output rows (and text partials) are 32-byte aligned
-    // fused tcgen05 path of a layer sharded over GPUs: every video row is also
-    // stored, at the same element offset, into these peers' output buffers
-    // (P2P stores over NVLink; the buffers are mapped into this process)
-    static constexpr int kMaxPeers = 7;
-    void* peer_out[kMaxPeers] = {};
-    int peer_count = 0;
 };
 
 // Launchers (return a cudaError_t value as int).
@@ -147,22 +141,19 @@ int launch_out_project(int tokens, int k_dim, int n_out, const void* x, int64_t 
 
 int* device_error_flag();  // per-device flag in device memory
 
-// awa_forward_windows whose tcgen05 kernel also stores every video row into
-// peer_out[0..peer_count) (peer buffers at the same element offsets as
-// video_out). Returns the kernel kind's status; peers need the tcgen05 kernel.
-int forward_windows_to_peers(const awa_plan* plan, int precision, int heads, int head_dim, int window_begin,
-                             int window_end, int in_dtype, const void* video_qkv, int64_t video_token_stride,
-                             int64_t video_qkv_stride, const void* text_qkv, int64_t text_token_stride,
-                             int64_t text_qkv_stride, int out_dtype, void* video_out, int64_t video_token_stride_out,
-                             float* text_partial, void* workspace, size_t workspace_bytes,
-                             void* const* peer_out, int peer_count, cudaStream_t stream);
-// awa_forward (all windows; heads and pointers as given) whose tcgen05 kernel
-// also stores every video row into the peers' buffers.
-int forward_to_peers(const awa_plan* plan, int precision, int heads, int head_dim, int in_dtype,
-                     const void* video_qkv, int64_t video_token_stride, int64_t video_qkv_stride, const void* text_qkv,
-                     int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype, void* video_out,
-                     int64_t video_token_stride_out, void* text_out, int64_t text_token_stride_out, void* workspace,
-                     size_t workspace_bytes, void* const* peer_out, int peer_count, cudaStream_t stream);
+// The fused attention kernel alone over windows [window_begin, window_end):
+// video rows into video_out, each window's text rows into the dense partials
+// (window w at slot w - window_begin, of *partial_dtype: bf16 from the tcgen05
+// kernel, fp32 from the SIMT kernel). partial_bytes bounds the slots.
+int attention_range(const awa_plan* plan, int precision, int heads, int head_dim, int window_begin, int window_end,
+                    int in_dtype, const void* video_qkv, int64_t video_token_stride, int64_t video_qkv_stride,
+                    const void* text_qkv, int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype,
+                    void* video_out, int64_t video_token_stride_out, void* partials, size_t partial_bytes,
+                    int* partial_dtype, cudaStream_t stream);
+// fp32 sum over windows [window_begin, window_end) of dense partials (slot
+// w - window_begin), in window order, not divided.
+int text_partial_sum(const awa_plan* plan, int heads, int head_dim, int partial_dtype, const void* partials,
+                     int window_begin, int window_end, float* sum, cudaStream_t stream);
 // Sets the calling thread's awa_last_error() text; returns code.
 int report_error(int code, const char* message);
 

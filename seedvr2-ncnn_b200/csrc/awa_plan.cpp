@@ -745,7 +745,7 @@ static int forward_impl(const awa_plan* cplan, int precision, int heads, int hea
                         int window_end, int in_dtype, const void* video_qkv, int64_t vts, int64_t vqs,
                         const void* text_qkv, int64_t tts, int64_t tqs, int out_dtype, void* video_out,
                         int64_t vots, void* workspace, size_t workspace_bytes, int* partial_dtype,
-                        cudaStream_t stream, void* const* peer_out = nullptr, int peer_count = 0)
+                        cudaStream_t stream)
 {
     awa_plan* plan = const_cast<awa_plan*>(cplan);
     const int64_t head_row = (int64_t)heads * head_dim;
@@ -782,15 +782,6 @@ static int forward_impl(const awa_plan* cplan, int precision, int heads, int hea
     args.out_token_stride = vots;
     args.text_partial = static_cast<float*>(workspace);
     args.window_begin = window_begin;
-    if (peer_count > 0)
-    {
-        if (!tc || peer_count > awa::AttnArgs::kMaxPeers || !peer_out)
-            return fail(AWA_ERR_INVALID, "awa_forward_sharded: peer stores need the tensor-core kernel and <= %d peers",
-                        awa::AttnArgs::kMaxPeers);
-        for (int p = 0; p < peer_count; p++)
-            args.peer_out[p] = peer_out[p];
-        args.peer_count = peer_count;
-    }
     int count = 0, rc = AWA_OK;
     const int2* items = range_items(plan, tc, window_begin, window_end, &count, &rc);
     if (rc)
@@ -855,58 +846,39 @@ int awa_forward_windows(const awa_plan* plan, int precision, int heads, int head
 namespace awa
 {
 
-int forward_windows_to_peers(const awa_plan* plan, int precision, int heads, int head_dim, int window_begin,
-                             int window_end, int in_dtype, const void* video_qkv, int64_t video_token_stride,
-                             int64_t video_qkv_stride, const void* text_qkv, int64_t text_token_stride,
-                             int64_t text_qkv_stride, int out_dtype, void* video_out, int64_t video_token_stride_out,
-                             float* text_partial, void* workspace, size_t workspace_bytes,
-                             void* const* peer_out, int peer_count, cudaStream_t stream)
+int attention_range(const awa_plan* plan, int precision, int heads, int head_dim, int window_begin, int window_end,
+                    int in_dtype, const void* video_qkv, int64_t video_token_stride, int64_t video_qkv_stride,
+                    const void* text_qkv, int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype,
+                    void* video_out, int64_t video_token_stride_out, void* partials, size_t partial_bytes,
+                    int* partial_dtype, cudaStream_t stream)
 {
     int rc = check_heads(plan, heads, head_dim);
     if (rc)
         return rc;
-    if (window_begin < 0 || window_end > plan->info.window_count || window_begin > window_end || !text_partial)
-        return fail(AWA_ERR_INVALID, "awa_forward_sharded: invalid window range [%d, %d)", window_begin, window_end);
+    if (window_begin < 0 || window_end > plan->info.window_count || window_begin > window_end || !partial_dtype)
+        return fail(AWA_ERR_INVALID, "attention range [%d, %d) invalid", window_begin, window_end);
+    *partial_dtype = awa_attention_kernel_kind(plan, precision, in_dtype, heads, head_dim) == 1 ? AWA_BF16 : AWA_F32;
     if (window_begin == window_end)
-        return launch_status(cudaMemsetAsync(text_partial, 0,
-                                             (size_t)plan->info.text_tokens * heads * head_dim * sizeof(float), stream),
-                             "memset text partial");
-    int partial_dtype = AWA_F32;
-    rc = forward_impl(plan, precision, heads, head_dim, window_begin, window_end, in_dtype, video_qkv,
-                      video_token_stride, video_qkv_stride, text_qkv, text_token_stride, text_qkv_stride, out_dtype,
-                      video_out, video_token_stride_out, workspace, workspace_bytes, &partial_dtype, stream, peer_out,
-                      peer_count);
-    if (rc)
-        return rc;
-    return launch_status(awa::launch_text_reduce(plan->dev, heads, head_dim, 0, partial_dtype, workspace,
-                                                 (int64_t)heads * head_dim, window_begin, window_end, 0.f, AWA_F32,
-                                                 text_partial, (int64_t)heads * head_dim, stream),
-                         "awa_forward_sharded text partial");
+        return AWA_OK;
+    return forward_impl(plan, precision, heads, head_dim, window_begin, window_end, in_dtype, video_qkv,
+                        video_token_stride, video_qkv_stride, text_qkv, text_token_stride, text_qkv_stride, out_dtype,
+                        video_out, video_token_stride_out, partials, partial_bytes, partial_dtype, stream);
 }
 
-int forward_to_peers(const awa_plan* plan, int precision, int heads, int head_dim, int in_dtype,
-                     const void* video_qkv, int64_t video_token_stride, int64_t video_qkv_stride, const void* text_qkv,
-                     int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype, void* video_out,
-                     int64_t video_token_stride_out, void* text_out, int64_t text_token_stride_out, void* workspace,
-                     size_t workspace_bytes, void* const* peer_out, int peer_count, cudaStream_t stream)
+int text_partial_sum(const awa_plan* plan, int heads, int head_dim, int partial_dtype, const void* partials,
+                     int window_begin, int window_end, float* sum, cudaStream_t stream)
 {
     int rc = check_heads(plan, heads, head_dim);
     if (rc)
         return rc;
-    if (!text_out || text_token_stride_out < (int64_t)heads * head_dim)
-        return fail(AWA_ERR_INVALID, "awa_forward_sharded: invalid text output");
-    int partial_dtype = AWA_F32;
-    rc = forward_impl(plan, precision, heads, head_dim, 0, plan->info.window_count, in_dtype, video_qkv,
-                      video_token_stride, video_qkv_stride, text_qkv, text_token_stride, text_qkv_stride, out_dtype,
-                      video_out, video_token_stride_out, workspace, workspace_bytes, &partial_dtype, stream, peer_out,
-                      peer_count);
-    if (rc)
-        return rc;
-    return launch_status(awa::launch_text_reduce(plan->dev, heads, head_dim, 0, partial_dtype, workspace,
-                                                 (int64_t)heads * head_dim, 0, plan->info.window_count,
-                                                 (float)plan->info.window_count, out_dtype, text_out,
-                                                 text_token_stride_out, stream),
-                         "awa_forward_sharded text reduce");
+    if (window_begin == window_end)
+        return launch_status(cudaMemsetAsync(sum, 0, (size_t)plan->info.text_tokens * heads * head_dim * sizeof(float),
+                                             stream),
+                             "memset text partial");
+    return launch_status(awa::launch_text_reduce(plan->dev, heads, head_dim, 0, partial_dtype, partials,
+                                                 (int64_t)heads * head_dim, window_begin, window_end, 0.f, AWA_F32,
+                                                 sum, (int64_t)heads * head_dim, stream),
+                         "text partial sum");
 }
 
 }  // namespace awa

@@ -136,6 +136,8 @@ struct awa_comm
     bool owned = false;
     std::vector<SharedBuffer> shared;
     int* barrier_word = nullptr;  // device int for the entry barrier of the direct mode
+    cudaStream_t push_stream = nullptr;  // direct mode: peer copies of video rows
+    cudaEvent_t push_events[8] = {};     // per chunk, and the join
 };
 
 namespace
@@ -236,6 +238,120 @@ int barrier(const Nccl* n, awa_comm* c, cudaStream_t stream)
 {
     return nccl_status(n, n->all_reduce(c->barrier_word, c->barrier_word, 1, ncclInt32, ncclSum, c->comm, stream),
                        "ncclAllReduce (barrier)");
+}
+
+// ---------------------------------------------------------------- direct mode pushes
+constexpr int kPushChunks = 4;  // attention launches per rank, each followed by its rows' peer copies
+
+// The side stream and events of the peer copies (made once per communicator).
+int push_streams(awa_comm* c)
+{
+    if (c->push_stream)
+        return AWA_OK;
+    cudaError_t e = cudaStreamCreateWithFlags(&c->push_stream, cudaStreamNonBlocking);
+    for (int i = 0; i < kPushChunks + 1 && e == cudaSuccess; i++)
+        e = cudaEventCreateWithFlags(&c->push_events[i], cudaEventDisableTiming);
+    return cuda_status(e, "peer copy stream");
+}
+
+// Chunk boundaries of windows [w0, w1): up to kPushChunks runs of near-equal
+// attention cost (sum of L^2, L = video rows; the text rows add the same to
+// every window of one shape).
+std::vector<int> push_chunks(const std::vector<awa_window>& win, int w0, int w1)
+{
+    std::vector<double> cost;
+    double total = 0;
+    for (int w = w0; w < w1; w++)
+    {
+        const double L = (double)(win[w].t1 - win[w].t0) * (win[w].h1 - win[w].h0) * (win[w].w1 - win[w].w0);
+        cost.push_back(L * L);
+        total += L * L;
+    }
+    const int chunks = std::max(1, std::min(kPushChunks, (w1 - w0) / 8));
+    std::vector<int> cuts{w0};
+    double acc = 0;
+    int w = w0;
+    for (int c = 1; c < chunks; c++)
+    {
+        while (w < w1 && acc + 0.5 * cost[w - w0] < total * c / chunks)
+            acc += cost[w++ - w0];
+        if (w > cuts.back())
+            cuts.push_back(w);
+    }
+    if (w1 > cuts.back())
+        cuts.push_back(w1);
+    return cuts;
+}
+
+// Copies the video rows of windows [wb, we) from `local` into every peer, on
+// the side stream once the attention that wrote them (enqueued on `st`) is
+// done. Windows in plan order run t fastest, then h, then w: runs of windows
+// are merged into boxes (t0..t1, h0..h1, w0..w1) first along t, then h, then w,
+// and each box goes as one pitched copy per frame per peer.
+int push_rows(awa_comm* c, const std::vector<awa_window>& win, int wb, int we, unsigned char* local,
+              const std::vector<unsigned char*>& peers, int64_t line_bytes, int64_t frame_bytes, int64_t token_bytes,
+              int64_t row_bytes, size_t chunk, cudaStream_t st)
+{
+    std::vector<awa_window> boxes;
+    for (int w = wb; w < we; w++)
+    {
+        const awa_window& x = win[w];
+        if (!boxes.empty())
+        {
+            awa_window& b = boxes.back();
+            if (b.h0 == x.h0 && b.h1 == x.h1 && b.w0 == x.w0 && b.w1 == x.w1 && b.t1 == x.t0)
+            {
+                b.t1 = x.t1;
+                continue;
+            }
+            if (b.t0 == x.t0 && b.t1 == x.t1 && b.w0 == x.w0 && b.w1 == x.w1 && b.h1 == x.h0)
+            {
+                b.h1 = x.h1;
+                continue;
+            }
+        }
+        boxes.push_back(x);
+    }
+    // boxes that follow each other along w
+    std::vector<awa_window> merged;
+    for (const awa_window& x : boxes)
+    {
+        if (!merged.empty())
+        {
+            awa_window& b = merged.back();
+            if (b.t0 == x.t0 && b.t1 == x.t1 && b.h0 == x.h0 && b.h1 == x.h1 && b.w1 == x.w0)
+            {
+                b.w1 = x.w1;
+                continue;
+            }
+        }
+        merged.push_back(x);
+    }
+    cudaError_t e = cudaEventRecord(c->push_events[chunk], st);
+    if (e == cudaSuccess)
+        e = cudaStreamWaitEvent(c->push_stream, c->push_events[chunk], 0);
+    for (const awa_window& b : merged)
+    {
+        const int64_t width = (int64_t)(b.w1 - b.w0 - 1) * token_bytes + row_bytes;
+        for (int t = b.t0; t < b.t1 && e == cudaSuccess; t++)
+        {
+            const int64_t off = t * frame_bytes + b.h0 * line_bytes + b.w0 * token_bytes;
+            for (unsigned char* peer : peers)
+                if (e == cudaSuccess)
+                    e = cudaMemcpy2DAsync(peer + off, line_bytes, local + off, line_bytes, width, b.h1 - b.h0,
+                                          cudaMemcpyDeviceToDevice, c->push_stream);
+        }
+    }
+    return cuda_status(e, "peer copy of video rows");
+}
+
+// `st` waits for every peer copy issued so far.
+int join_pushes(awa_comm* c, cudaStream_t st)
+{
+    cudaError_t e = cudaEventRecord(c->push_events[kPushChunks], c->push_stream);
+    if (e == cudaSuccess)
+        e = cudaStreamWaitEvent(st, c->push_events[kPushChunks], 0);
+    return cuda_status(e, "peer copy join");
 }
 
 }  // namespace
@@ -415,6 +531,11 @@ void awa_comm_destroy(awa_comm* comm)
         release_shared(b, comm->rank);
     if (comm->barrier_word)
         cudaFree(comm->barrier_word);
+    for (cudaEvent_t e : comm->push_events)
+        if (e)
+            cudaEventDestroy(e);
+    if (comm->push_stream)
+        cudaStreamDestroy(comm->push_stream);
     const Nccl* n = nccl();
     if (comm->owned && comm->comm && n)
         n->comm_destroy(comm->comm);
@@ -464,7 +585,7 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
     if (!plan || !comm || awa_plan_get_info(plan, &info) != AWA_OK)
         return fail(AWA_ERR_INVALID, "awa_forward_sharded: NULL plan or communicator");
     if (heads <= 0 || head_dim <= 0 || !video_qkv || !text_qkv || !video_out || !text_out || !workspace ||
-        (out_dtype != AWA_F32 && out_dtype != AWA_BF16))
+        (out_dtype != AWA_F32 && out_dtype != AWA_BF16) || video_token_stride_out < (int64_t)heads * head_dim)
         return fail(AWA_ERR_INVALID, "awa_forward_sharded: invalid arguments");
     int device = -1;
     if (cudaGetDevice(&device) != cudaSuccess || device != comm->device || device != info.device)
@@ -485,29 +606,28 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
     const int64_t row = (int64_t)heads * head_dim;
     int rc = AWA_OK;
 
-    // Direct mode: video_out lies in a buffer shared over the ranks and the
-    // tensor-core kernel runs. The kernel then stores each video row into every
-    // rank's copy of video_out as it computes it (P2P stores over NVLink), so
-    // the video rows need no all-gather, staging or scatter. An entry barrier
-    // keeps any rank from writing before every rank has finished with the
-    // previous contents; the text collective at the end orders the stores
-    // before every rank's later reads.
+    // Direct mode: video_out lies in a buffer shared over the ranks. The copy
+    // engines then push this rank's video rows into every other rank's copy of
+    // video_out over NVLink (peer copies on a side stream), chunk by chunk as
+    // the attention kernel finishes them, so the transfer overlaps the next
+    // chunk's attention and needs no all-gather, staging or scatter. An entry
+    // barrier keeps any rank from writing before every rank is done with the
+    // previous contents; the text collective at the end, enqueued after the
+    // copies, orders them before every rank's later reads.
     const size_t video_span = (size_t)(info.source_tokens - 1) * video_token_stride_out * osz + (size_t)row * osz;
     const SharedBuffer* shared = find_shared(comm, video_out, video_span);
-    const int head_hint = s.by_heads ? s.bounds[1] - s.bounds[0] : heads;
-    const bool direct = shared && R - 1 <= awa::AttnArgs::kMaxPeers &&
-                        awa_attention_kernel_kind(plan, precision, in_dtype, std::max(head_hint, 1), head_dim) == 1;
-    std::vector<void*> peers;
+    const bool direct = shared != nullptr && R > 1;
+    std::vector<unsigned char*> peers;  // the other ranks' video_out
     if (direct)
     {
         const size_t off = static_cast<unsigned char*>(video_out) - static_cast<unsigned char*>(shared->local);
         for (int q = 0; q < R; q++)
             if (q != r)
                 peers.push_back(static_cast<unsigned char*>(shared->peer[q]) + off);
-        rc = barrier(n, comm, st);
-        if (rc)
+        if ((rc = push_streams(comm)) != AWA_OK || (rc = barrier(n, comm, st)) != AWA_OK)
             return rc;
     }
+    const int64_t line_bytes = (int64_t)info.source_w * video_token_stride_out * osz;  // one grid line of tokens
 
     if (s.by_heads)
     {
@@ -517,33 +637,34 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
         for (int q = 0; q < R; q++)
             most = std::max(most, s.bounds[q + 1] - s.bounds[q]);
         const size_t hoff_in = (size_t)h0 * head_dim * isz, hoff_out = (size_t)h0 * head_dim * osz;
-        std::vector<void*> head_peers;
-        for (void* p : peers)
-            head_peers.push_back(static_cast<unsigned char*>(p) + hoff_out);
         if (hn > 0)
-            rc = awa::forward_to_peers(plan, precision, hn, head_dim, in_dtype,
-                                       static_cast<const unsigned char*>(video_qkv) + hoff_in, video_token_stride,
-                                       video_qkv_stride, static_cast<const unsigned char*>(text_qkv) + hoff_in,
-                                       text_token_stride, text_qkv_stride, out_dtype,
-                                       static_cast<unsigned char*>(video_out) + hoff_out, video_token_stride_out,
-                                       static_cast<unsigned char*>(text_out) + hoff_out, text_token_stride_out,
-                                       ws + l.forward, l.gather - l.forward, head_peers.data(),
-                                       (int)head_peers.size(), st);
+            rc = awa_forward(plan, precision, hn, head_dim, in_dtype,
+                             static_cast<const unsigned char*>(video_qkv) + hoff_in, video_token_stride,
+                             video_qkv_stride, static_cast<const unsigned char*>(text_qkv) + hoff_in,
+                             text_token_stride, text_qkv_stride, out_dtype,
+                             static_cast<unsigned char*>(video_out) + hoff_out, video_token_stride_out,
+                             static_cast<unsigned char*>(text_out) + hoff_out, text_token_stride_out,
+                             ws + l.forward, l.gather - l.forward, stream);
         if (rc)
             return rc;
-        // Pack this rank's head slices into its slots ([N_v][most][d] and [T][most][d]).
         const size_t vslot = (size_t)info.source_tokens * most * head_dim, tslot = (size_t)info.text_tokens * most * head_dim;
         unsigned char* vg = ws + l.gather;
         unsigned char* tg = ws + l.text_gather;
         const size_t width = (size_t)hn * head_dim * osz, spitch = (size_t)most * head_dim * osz;
-        if (hn > 0 && !direct)
-        {
+        const size_t vpitch = (size_t)video_token_stride_out * osz;
+        if (hn > 0 && direct)
+            // the head slice of every token row, into every peer's output
+            for (unsigned char* peer : peers)
+                if (rc == AWA_OK)
+                    rc = cuda_status(cudaMemcpy2DAsync(peer + hoff_out, vpitch,
+                                                       static_cast<unsigned char*>(video_out) + hoff_out, vpitch,
+                                                       width, info.source_tokens, cudaMemcpyDeviceToDevice, st),
+                                     "head slice push (video)");
+        if (hn > 0 && !direct && rc == AWA_OK)
             rc = cuda_status(cudaMemcpy2DAsync(vg + r * vslot * osz, spitch,
-                                               static_cast<unsigned char*>(video_out) + hoff_out,
-                                               video_token_stride_out * osz, width, info.source_tokens,
-                                               cudaMemcpyDeviceToDevice, st),
+                                               static_cast<unsigned char*>(video_out) + hoff_out, vpitch, width,
+                                               info.source_tokens, cudaMemcpyDeviceToDevice, st),
                              "head slice pack (video)");
-        }
         if (hn > 0 && rc == AWA_OK)
             rc = cuda_status(cudaMemcpy2DAsync(tg + r * tslot * osz, spitch,
                                                static_cast<unsigned char*>(text_out) + hoff_out,
@@ -554,13 +675,13 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
             return rc;
         rc = nccl_status(n, n->group_start(), "ncclGroupStart");
         if (rc == AWA_OK && !direct)
-            rc = nccl_status(n, n->all_gather(vg + r * vslot * osz, vg, vslot, otype, comm->comm, st), "ncclAllGather (video)");
+            rc = nccl_status(n, n->all_gather(vg + r * vslot * osz, vg, vslot, otype, comm->comm, st),
+                             "ncclAllGather (video)");
         if (rc == AWA_OK)
-            rc = nccl_status(n, n->all_gather(tg + r * tslot * osz, tg, tslot, otype, comm->comm, st), "ncclAllGather (text)");
+            rc = nccl_status(n, n->all_gather(tg + r * tslot * osz, tg, tslot, otype, comm->comm, st),
+                             "ncclAllGather (text)");
         const int end_rc = nccl_status(n, n->group_end(), "ncclGroupEnd");
         rc = rc ? rc : end_rc;
-        if (rc)
-            return rc;
         for (int q = 0; q < R && rc == AWA_OK; q++)
         {
             const int qn = s.bounds[q + 1] - s.bounds[q];
@@ -568,9 +689,9 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
                 continue;
             const size_t qoff = (size_t)s.bounds[q] * head_dim * osz, qwidth = (size_t)qn * head_dim * osz;
             if (!direct)
-                rc = cuda_status(cudaMemcpy2DAsync(static_cast<unsigned char*>(video_out) + qoff,
-                                                   video_token_stride_out * osz, vg + q * vslot * osz, spitch, qwidth,
-                                                   info.source_tokens, cudaMemcpyDeviceToDevice, st),
+                rc = cuda_status(cudaMemcpy2DAsync(static_cast<unsigned char*>(video_out) + qoff, vpitch,
+                                                   vg + q * vslot * osz, spitch, qwidth, info.source_tokens,
+                                                   cudaMemcpyDeviceToDevice, st),
                                  "head slice unpack (video)");
             if (rc == AWA_OK)
                 rc = cuda_status(cudaMemcpy2DAsync(static_cast<unsigned char*>(text_out) + qoff,
@@ -584,21 +705,48 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
     // Window split: this rank's windows [w0, w1).
     const int w0 = s.bounds[r], w1 = s.bounds[r + 1];
     float* text_sum = reinterpret_cast<float*>(ws + l.text_sum);
-    rc = awa::forward_windows_to_peers(plan, precision, heads, head_dim, w0, w1, in_dtype, video_qkv,
-                                       video_token_stride, video_qkv_stride, text_qkv, text_token_stride,
-                                       text_qkv_stride, out_dtype, video_out, video_token_stride_out, text_sum,
-                                       ws + l.forward, l.gather - l.forward, peers.data(), (int)peers.size(), st);
-    if (rc)
-        return rc;
+    unsigned char* partials = ws + l.forward;
+    const size_t partial_bytes = l.gather - l.forward;
+    const size_t window_partial = (size_t)info.text_tokens * row;  // elements per window
+    int partial_dtype = AWA_F32;
     if (direct)
     {
-        rc = nccl_status(n, n->all_reduce(text_sum, text_sum, (size_t)info.text_tokens * row, ncclFloat32, ncclSum,
-                                          comm->comm, st),
-                         "ncclAllReduce (text partial sums)");
+        std::vector<awa_window> windows(info.window_count);
+        awa_plan_get_maps(plan, nullptr, nullptr, nullptr, nullptr, windows.data());
+        const std::vector<int> cuts = push_chunks(windows, w0, w1);
+        for (size_t c = 0; c + 1 < cuts.size() && rc == AWA_OK; c++)
+        {
+            const int cb = cuts[c], ce = cuts[c + 1];
+            int pd = AWA_F32;
+            const size_t psz_guess = awa_attention_kernel_kind(plan, precision, in_dtype, heads, head_dim) == 1 ? 2 : 4;
+            const size_t off = (size_t)(cb - w0) * window_partial * psz_guess;
+            rc = awa::attention_range(plan, precision, heads, head_dim, cb, ce, in_dtype, video_qkv,
+                                      video_token_stride, video_qkv_stride, text_qkv, text_token_stride,
+                                      text_qkv_stride, out_dtype, video_out, video_token_stride_out, partials + off,
+                                      partial_bytes - off, &pd, st);
+            partial_dtype = pd;
+            if (rc == AWA_OK)
+                rc = push_rows(comm, windows, cb, ce, static_cast<unsigned char*>(video_out), peers, line_bytes,
+                               (int64_t)info.source_h * line_bytes, video_token_stride_out * osz, row * osz, c, st);
+        }
+        if (rc == AWA_OK)
+            rc = awa::text_partial_sum(plan, heads, head_dim, partial_dtype, partials, w0, w1, text_sum, st);
+        if (rc == AWA_OK)
+            rc = join_pushes(comm, st);
+        if (rc == AWA_OK)
+            rc = nccl_status(n, n->all_reduce(text_sum, text_sum, (size_t)info.text_tokens * row, ncclFloat32, ncclSum,
+                                              comm->comm, st),
+                             "ncclAllReduce (text partial sums)");
         if (rc)
             return rc;
         return awa_text_finalize(plan, heads, head_dim, text_sum, out_dtype, text_out, text_token_stride_out, stream);
     }
+
+    rc = awa_forward_windows(plan, precision, heads, head_dim, w0, w1, in_dtype, video_qkv, video_token_stride,
+                             video_qkv_stride, text_qkv, text_token_stride, text_qkv_stride, out_dtype, video_out,
+                             video_token_stride_out, text_sum, partials, partial_bytes, stream);
+    if (rc)
+        return rc;
     unsigned char* gather = ws + l.gather;
     const size_t slot = (size_t)s.slot_rows * row;  // elements
     rc = awa_gather_video_shard(plan, heads, head_dim, w0, w1, out_dtype, video_out, video_token_stride_out,
