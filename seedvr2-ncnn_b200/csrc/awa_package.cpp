@@ -21,6 +21,7 @@
 #include <fstream>
 #include <iterator>
 #include <map>
+#include <set>
 #include <string>
 #include <system_error>
 #include <vector>
@@ -714,147 +715,227 @@ bool read_file(const char* path, std::string& data, std::string& error)
 }
 
 // ---------------------------------------------------------------- manifest
-bool is_hex_hash(const std::string& hash)
+// The package check of the reference's model registry
+// (src/model/model_registry.cpp:248-362), built here as three steps: read the
+// manifest into records, list the package's files with a walker of its own,
+// compare the two. The rules and the messages are the registry's (a package
+// must be accepted or refused the same way by both runtimes); the code is not.
+struct ManifestRecord
 {
-    if (hash.size() != 64)
+    std::string name;
+    std::string digest;  // lowercase hex
+};
+
+// A manifest path: relative, POSIX separators, no empty ("//"), "." or ".."
+// component and no backslash (the registry's safe_manifest_path, as
+// std::filesystem reads a path on POSIX: a single trailing '/' is allowed).
+bool manifest_path_ok(const std::string& name)
+{
+    if (name.empty() || name[0] == '/' || name.find('\\') != std::string::npos ||
+        name.find("//") != std::string::npos)
         return false;
-    for (unsigned char c : hash)
-        if (!std::isxdigit(c))
+    size_t begin = 0;
+    while (begin <= name.size())
+    {
+        size_t end = name.find('/', begin);
+        if (end == std::string::npos)
+            end = name.size();
+        const std::string part = name.substr(begin, end - begin);
+        if (part == "." || part == "..")
             return false;
+        begin = end + 1;
+    }
     return true;
 }
 
-bool safe_manifest_path(const std::string& name)
+int hex_value(char c)
 {
-    if (name.empty() || name.find('\\') != std::string::npos)
-        return false;
-    const std::filesystem::path path(name);
-    if (path.is_absolute() || path.has_root_name() || path.has_root_directory())
-        return false;
-    for (const auto& component : path)
-        if (component == ".." || component == ".")
-            return false;
-    return path.generic_string() == name;
+    if (c >= '0' && c <= '9')
+        return c - '0';
+    if (c >= 'a' && c <= 'f')
+        return c - 'a' + 10;
+    if (c >= 'A' && c <= 'F')
+        return c - 'A' + 10;
+    return -1;
 }
 
-bool validate_manifest(const std::filesystem::path& dir, int expected_records, std::string& error)
+// Reads manifest.sha256 into records sorted by name. A record line is 64 hex
+// digits, two spaces and a path; CR line ends and blank lines are allowed.
+bool read_manifest(const std::filesystem::path& file, std::vector<ManifestRecord>& records, std::string& error)
 {
-    const std::filesystem::path manifest = dir / "manifest.sha256";
-    std::ifstream input(manifest);
-    if (!input)
+    std::string text;
     {
-        error = "missing model package manifest: " + manifest.string();
-        return false;
+        std::ifstream input(file, std::ios::binary);
+        if (!input)
+        {
+            error = "missing model package manifest: " + file.string();
+            return false;
+        }
+        text.assign(std::istreambuf_iterator<char>(input), std::istreambuf_iterator<char>());
     }
-    std::map<std::string, std::string> expected;
-    size_t line_number = 0;
-    std::string line;
-    while (std::getline(input, line))
+    std::set<std::string> names;
+    size_t number = 0, pos = 0;
+    while (pos < text.size())
     {
-        ++line_number;
+        size_t stop = text.find('\n', pos);
+        if (stop == std::string::npos)
+            stop = text.size();
+        std::string line = text.substr(pos, stop - pos);
+        pos = stop + 1;
+        ++number;
         if (!line.empty() && line.back() == '\r')
             line.pop_back();
         if (line.empty())
             continue;
-        const size_t separator = line.find("  ");
-        if (separator != 64 || line.size() <= separator + 2 || !is_hex_hash(line.substr(0, separator)))
+        ManifestRecord rec;
+        bool hex = line.size() > 66 && line.compare(64, 2, "  ") == 0 && line.find("  ") == 64;
+        for (size_t i = 0; hex && i < 64; i++)
         {
-            error = "invalid model package manifest record at line " + std::to_string(line_number);
+            const int v = hex_value(line[i]);
+            hex = v >= 0;
+            rec.digest.push_back("0123456789abcdef"[v < 0 ? 0 : v]);
+        }
+        if (!hex)
+        {
+            error = "invalid model package manifest record at line " + std::to_string(number);
             return false;
         }
-        const std::string name = line.substr(separator + 2);
-        if (!safe_manifest_path(name))
+        rec.name = line.substr(66);
+        if (!manifest_path_ok(rec.name))
         {
-            error = "invalid model package manifest path at line " + std::to_string(line_number);
+            error = "invalid model package manifest path at line " + std::to_string(number);
             return false;
         }
-        std::string digest = line.substr(0, separator);
-        for (char& c : digest)
-            c = (char)std::tolower((unsigned char)c);
-        if (!expected.emplace(name, digest).second)
+        if (!names.insert(rec.name).second)
         {
-            error = "duplicate model package manifest path: " + name;
+            error = "duplicate model package manifest path: " + rec.name;
             return false;
         }
+        records.push_back(std::move(rec));
     }
-    if (expected_records == 0 && expected.size() != 75 && expected.size() != 146)
-    {
-        error = "model package manifest must contain 75 records (positive) or 146 records (positive + CFG), got " +
-                std::to_string(expected.size());
-        return false;
-    }
-    if (expected_records > 0 && expected.size() != (size_t)expected_records)
-    {
-        error = "model package manifest must contain " + std::to_string(expected_records) + " records, got " +
-                std::to_string(expected.size());
-        return false;
-    }
+    std::sort(records.begin(), records.end(),
+              [](const ManifestRecord& a, const ManifestRecord& b) { return a.name < b.name; });
+    return true;
+}
 
-    std::map<std::string, std::filesystem::path> actual;
-    std::error_code ec;
-    for (std::filesystem::recursive_directory_iterator it(dir, ec), end; it != end; it.increment(ec))
+// Every regular file under dir (except the top-level manifest) as
+// (relative POSIX name, path), sorted by name. Directories are entered, never
+// followed through links; any link is refused.
+bool list_package(const std::filesystem::path& dir, std::vector<std::pair<std::string, std::filesystem::path>>& files,
+                  std::string& error)
+{
+    namespace fs = std::filesystem;
+    const std::string inspect = "failed to inspect model package: " + dir.string();
+    std::vector<fs::path> pending{dir};
+    while (!pending.empty())
     {
+        const fs::path here = pending.back();
+        pending.pop_back();
+        std::error_code ec;
+        fs::directory_iterator it(here, ec), end;
         if (ec)
         {
-            error = "failed to inspect model package: " + dir.string();
+            error = inspect;
             return false;
         }
-        const bool is_symlink = it->is_symlink(ec);
-        if (ec)
-        {
-            error = "failed to inspect model package: " + dir.string();
-            return false;
-        }
-        if (is_symlink)
-        {
-            error = "model package must not contain symbolic links: " + it->path().string();
-            return false;
-        }
-        if (!it->is_regular_file(ec))
+        for (; it != end; it.increment(ec))
         {
             if (ec)
             {
-                error = "failed to inspect model package: " + dir.string();
+                error = inspect;
                 return false;
             }
-            continue;
+            const fs::file_status st = it->symlink_status(ec);
+            if (ec)
+            {
+                error = inspect;
+                return false;
+            }
+            if (fs::is_symlink(st))
+            {
+                error = "model package must not contain symbolic links: " + it->path().string();
+                return false;
+            }
+            if (fs::is_directory(st))
+                pending.push_back(it->path());
+            else if (fs::is_regular_file(st))
+            {
+                std::string name = it->path().lexically_relative(dir).generic_string();
+                if (name != "manifest.sha256")
+                    files.emplace_back(std::move(name), it->path());
+            }
         }
-        const std::string name = std::filesystem::relative(it->path(), dir).generic_string();
-        if (name == "manifest.sha256")
-            continue;
-        if (!actual.emplace(name, it->path()).second)
+        if (ec)
         {
-            error = "duplicate model package artifact path: " + name;
+            error = inspect;
             return false;
         }
     }
-    if (ec)
+    std::sort(files.begin(), files.end());
+    for (size_t i = 1; i < files.size(); i++)
+        if (files[i].first == files[i - 1].first)
+        {
+            error = "duplicate model package artifact path: " + files[i].first;
+            return false;
+        }
+    return true;
+}
+
+// expected_records: 0 = the registry's rule (75 records for a positive-only
+// package, 146 with the CFG branch), > 0 = exactly that many, < 0 = any.
+bool validate_manifest(const std::filesystem::path& dir, int expected_records, std::string& error)
+{
+    std::vector<ManifestRecord> records;
+    if (!read_manifest(dir / "manifest.sha256", records, error))
+        return false;
+    const size_t count = records.size();
+    if (expected_records == 0 && count != 75 && count != 146)
     {
-        error = "failed to inspect model package: " + dir.string();
+        error = "model package manifest must contain 75 records (positive) or 146 records (positive + CFG), got " +
+                std::to_string(count);
         return false;
     }
-    for (const auto& [name, digest] : expected)
+    if (expected_records > 0 && count != (size_t)expected_records)
     {
-        const auto found = actual.find(name);
-        if (found == actual.end())
+        error = "model package manifest must contain " + std::to_string(expected_records) + " records, got " +
+                std::to_string(count);
+        return false;
+    }
+    std::vector<std::pair<std::string, std::filesystem::path>> files;
+    if (!list_package(dir, files, error))
+        return false;
+    auto by_name = [](const std::pair<std::string, std::filesystem::path>& f, const std::string& n) {
+        return f.first < n;
+    };
+    // every record names a file whose digest it holds (records in name order) ...
+    for (const ManifestRecord& rec : records)
+    {
+        const auto hit = std::lower_bound(files.begin(), files.end(), rec.name, by_name);
+        if (hit == files.end() || hit->first != rec.name)
         {
-            error = "manifest artifact is missing: " + name;
+            error = "manifest artifact is missing: " + rec.name;
             return false;
         }
-        std::string actual_digest;
-        if (!sha256_file(found->second, actual_digest, error))
+        std::string digest;
+        if (!sha256_file(hit->second, digest, error))
             return false;
-        if (actual_digest != digest)
+        if (digest != rec.digest)
         {
-            error = "manifest hash mismatch for artifact: " + name;
+            error = "manifest hash mismatch for artifact: " + rec.name;
             return false;
         }
     }
-    for (const auto& [name, path] : actual)
-        if (expected.find(name) == expected.end())
+    // ... and no file is left out (files in name order)
+    if (files.size() != records.size())
+        for (const auto& f : files)
         {
-            error = "artifact is not listed in model package manifest: " + path.string();
-            return false;
+            const auto hit = std::lower_bound(records.begin(), records.end(), f.first,
+                                              [](const ManifestRecord& r, const std::string& n) { return r.name < n; });
+            if (hit == records.end() || hit->name != f.first)
+            {
+                error = "artifact is not listed in model package manifest: " + f.second.string();
+                return false;
+            }
         }
     return true;
 }

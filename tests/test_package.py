@@ -287,6 +287,8 @@ MANIFEST_FAULTS = {
     "absolute path": "invalid model package manifest path at line 6",
     "dot component": "invalid model package manifest path at line 6",
     "backslash": "invalid model package manifest path at line 6",
+    "double slash": "invalid model package manifest path at line 6",
+    "trailing slash": "manifest artifact is missing: sub/",
     "duplicate record": "duplicate model package manifest path: a.bin",
     "missing artifact": "manifest artifact is missing: zz.bin",
     "hash mismatch": "manifest hash mismatch for artifact: b.bin",
@@ -304,6 +306,8 @@ def test_manifest_rejects(fault, scratch):
         "absolute path": [f"{good}  /a.bin"],
         "dot component": [f"{good}  sub/./c.bin"],
         "backslash": [f"{good}  sub\\c.bin"],
+        "double slash": [f"{good}  sub//c.bin"],
+        "trailing slash": [f"{good}  sub/"],
         "duplicate record": [f"{hashlib.sha256(b'alpha').hexdigest()}  a.bin"],
         "missing artifact": [f"{good}  zz.bin"],
     }.get(fault, [])
