@@ -154,6 +154,16 @@ int awa_forward(const awa_plan* plan, int precision, int heads, int head_dim, in
                 int64_t video_token_stride_out, void* text_out, int64_t text_token_stride_out, void* workspace,
                 size_t workspace_bytes, awa_stream_t stream);
 
+/* awa_forward for Q/K rows that arrive rotated (awa_qkv_project_rotated with
+ * this plan): the chain without the MMRoPE step -- Pack, WindowAttention,
+ * Unpack. Same arguments, workspace and outputs as awa_forward. */
+int awa_forward_prerotated(const awa_plan* plan, int precision, int heads, int head_dim, int in_dtype,
+                           const void* video_qkv, int64_t video_token_stride, int64_t video_qkv_stride,
+                           const void* text_qkv, int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype,
+                           void* video_out, int64_t video_token_stride_out, void* text_out,
+                           int64_t text_token_stride_out, void* workspace, size_t workspace_bytes,
+                           awa_stream_t stream);
+
 /* Size of the scratch that awa_forward_noalloc uses: 32 MiB of device memory
  * per GPU that loads this library, held until the process exits. */
 #define AWA_NOALLOC_SCRATCH_BYTES (32u << 20)
@@ -295,6 +305,24 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
 int awa_qkv_project(int tokens, int model_dim, int heads, int head_dim, const void* x, int64_t x_stride,
                     const void* w, int64_t w_stride, const float* gamma_q, const float* gamma_k, float eps,
                     int out_dtype, void* out, int64_t out_stride, awa_stream_t stream);
+
+/* Branches of a DiT block's QKV projection (awa_qkv_project_rotated). */
+#define AWA_BRANCH_VIDEO 0
+#define AWA_BRANCH_TEXT 1
+
+/* awa_qkv_project with the layer's MMRoPE (SeedVR2MMRoPE, awa_layers.cpp:
+ * 867-953) in its epilogue: after the RMSNorm, each Q and K head of token row
+ * i is rotated in fp32 with the window-local coordinates the plan gives that
+ * token -- (text_tokens + t - t0, h - h0, w - w0) of its window for the video
+ * branch (tokens = the plan's video tokens, source order), (i, i, i) for the
+ * text branch (tokens = the plan's text tokens) -- and rounded once to
+ * out_dtype. The plan is the block's AWA layer plan (its shift decides the
+ * windows). The rows then go to awa_forward_prerotated, which skips the
+ * rotation. */
+int awa_qkv_project_rotated(int tokens, int model_dim, int heads, int head_dim, const void* x, int64_t x_stride,
+                            const void* w, int64_t w_stride, const float* gamma_q, const float* gamma_k, float eps,
+                            const awa_plan* plan, int branch, int out_dtype, void* out, int64_t out_stride,
+                            awa_stream_t stream);
 
 /* The consumer of the AWA output, on the tensor cores: for one branch of a DiT
  * block, proj_out (a Linear with bias, tools/reference/dit_block.py:299), the

@@ -32,12 +32,14 @@ AWA_ERR_CUDA = -2
 AWA_ERR_DEVICE = -3
 AWA_ERR_ALLOC = -100
 AWA_NOALLOC_SCRATCH_BYTES = 32 << 20  # scratch of awa_forward_noalloc, per GPU
+AWA_BRANCH_VIDEO = 0
+AWA_BRANCH_TEXT = 1
 
 # Every symbol declared in include/awa_b200.h, include/awa_package.h and include/awa_stack.h.
 EXPORTED_SYMBOLS = (
     "awa_make_windows", "awa_plan_create", "awa_plan_create_host", "awa_plan_destroy", "awa_plan_get_info", "awa_plan_get_maps",
     "awa_pack", "awa_mmrope", "awa_window_attention", "awa_unpack", "awa_forward_workspace_bytes", "awa_forward",
-    "awa_forward_noalloc",
+    "awa_forward_noalloc", "awa_forward_prerotated", "awa_qkv_project_rotated",
     "awa_forward_windows", "awa_text_finalize", "awa_scatter_video_shard", "awa_gather_video_shard",
     "awa_window_range_video_rows", "awa_partition_windows", "awa_qkv_project", "awa_out_project", "awa_device_status",
     "awa_selftest_bounded_wait", "awa_attention_kernel_kind",
@@ -124,6 +126,8 @@ def library() -> ctypes.CDLL:
         "awa_forward_workspace_bytes": (sz, [p, i, i]),
         "awa_forward": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p, sz, p]),
         "awa_forward_noalloc": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p]),
+        "awa_forward_prerotated": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p, sz, p]),
+        "awa_qkv_project_rotated": (i, [i, i, i, i, p, i64, p, i64, p, p, ctypes.c_float, p, i, i, p, i64, p]),
         "awa_qkv_project": (i, [i, i, i, i, p, i64, p, i64, p, p, ctypes.c_float, i, p, i64, p]),
         "awa_out_project": (i, [i, i, i, p, i64, p, i64, p, p, p, i64, i, i, p, i64, p]),
         "awa_forward_windows": (i, [p, i, i, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, p, sz, p]),
@@ -363,6 +367,28 @@ class AwaPlan:
                                      _stream_ptr(stream)))
         return video_out, text_out
 
+    def forward_prerotated(self, video_qkv, text_qkv, precision=AWA_PREC_BF16, out_dtype=None, workspace=None,
+                           video_out=None, text_out=None, stream=None):
+        """forward() for Q/K rows already rotated by qkv_project_rotated with this plan."""
+        torch = _torch()
+        heads, hd = video_qkv.shape[2], video_qkv.shape[3]
+        dt = video_qkv.dtype if out_dtype is None else out_dtype
+        if video_out is None:
+            video_out = torch.empty(self.info.source_tokens, heads, hd, dtype=dt, device=video_qkv.device)
+        if text_out is None:
+            text_out = torch.empty(self.info.text_tokens, heads, hd, dtype=dt, device=video_qkv.device)
+        if workspace is None:
+            workspace = torch.empty(max(self.workspace_bytes(heads, hd), 16), dtype=torch.uint8,
+                                    device=video_qkv.device)
+        vts, vqs = _qkv_strides(video_qkv)
+        tts, tqs = _qkv_strides(text_qkv)
+        _check(library().awa_forward_prerotated(self._handle, precision, heads, hd, _dtype_code(video_qkv),
+                                                video_qkv.data_ptr(), vts, vqs, text_qkv.data_ptr(), tts, tqs,
+                                                _dtype_code(video_out), video_out.data_ptr(), video_out.stride(0),
+                                                text_out.data_ptr(), text_out.stride(0), workspace.data_ptr(),
+                                                workspace.numel() * workspace.element_size(), _stream_ptr(stream)))
+        return video_out, text_out
+
     def forward_windows(self, video_qkv, text_qkv, window_begin: int, window_end: int, video_out, text_partial,
                         precision=AWA_PREC_BF16, workspace=None, stream=None):
         """Windows [begin, end) only: writes their video rows and the fp32 text partial sum."""
@@ -467,6 +493,24 @@ def qkv_project(x, w, gamma_q, gamma_k, eps: float, heads: int, out_dtype=None, 
     _check(library().awa_qkv_project(tokens, model_dim, heads, 128, x.data_ptr(), x.stride(0), w.data_ptr(),
                                      w.stride(0), gamma_q.data_ptr(), gamma_k.data_ptr(), float(eps),
                                      _dtype_code(out), out.data_ptr(), out.stride(0), _stream_ptr(stream)))
+    return out
+
+
+def qkv_project_rotated(x, w, gamma_q, gamma_k, eps: float, heads: int, plan: "AwaPlan", branch: int,
+                        out_dtype=None, out=None, stream=None):
+    """qkv_project with the layer's MMRoPE in the epilogue
+    (awa_qkv_project_rotated): Q and K heads rotated in fp32 with the
+    window-local coordinates `plan` gives each row of `branch`
+    (AWA_BRANCH_VIDEO: the plan's video tokens; AWA_BRANCH_TEXT: its text
+    tokens), rounded once. The rows feed AwaPlan.forward_prerotated."""
+    torch = _torch()
+    tokens, model_dim = x.shape
+    if out is None:
+        out = torch.empty(tokens, 3, heads, 128, dtype=out_dtype or torch.bfloat16, device=x.device)
+    _check(library().awa_qkv_project_rotated(tokens, model_dim, heads, 128, x.data_ptr(), x.stride(0), w.data_ptr(),
+                                             w.stride(0), gamma_q.data_ptr(), gamma_k.data_ptr(), float(eps),
+                                             plan.handle, branch, _dtype_code(out), out.data_ptr(), out.stride(0),
+                                             _stream_ptr(stream)))
     return out
 
 
@@ -792,6 +836,7 @@ def sha256_file(path) -> str:
 
 
 __all__ = ["AwaPlan", "AwaComm", "AwaError", "PlanInfo", "library", "make_windows", "device_status", "ncnn_run_chain",
-           "EXPORTED_SYMBOLS", "qkv_project", "out_project", "graph_find_chains", "graph_find_chains_file",
+           "EXPORTED_SYMBOLS", "qkv_project", "qkv_project_rotated", "out_project", "graph_find_chains", "graph_find_chains_file",
            "graph_make_dynamic", "manifest_validate", "sha256", "sha256_file", "AwaStack", "StackGraph", "StackIO",
-           "AWA_STACK_BEFORE", "AWA_STACK_AFTER", "AWA_F32", "AWA_BF16", "AWA_PREC_FP32", "AWA_PREC_BF16"]
+           "AWA_STACK_BEFORE", "AWA_STACK_AFTER", "AWA_F32", "AWA_BF16", "AWA_PREC_FP32", "AWA_PREC_BF16",
+           "AWA_BRANCH_VIDEO", "AWA_BRANCH_TEXT"]

@@ -85,7 +85,7 @@ __device__ __forceinline__ void load_transposed(const AttnArgs& a, float* tile, 
             if (p && 8 * c < hd)
             {
                 load8(p + qkv * step[row] + 8 * c, v);
-                if (ROPE)
+                if (ROPE && a.rotate)
                     rope8(a.plan, coords[row], 8 * c, v);
             }
 #pragma unroll
@@ -102,7 +102,7 @@ __device__ __forceinline__ void load_transposed(const AttnArgs& a, float* tile, 
             {
                 const TIn* seg = p + qkv * step[row];
                 v = load1(seg + f);
-                if (ROPE && f < a.plan.rope_dim)
+                if (ROPE && a.rotate && f < a.plan.rope_dim)
                 {
                     const float paired = load1(seg + (f ^ 1));
                     const float2 cs = rope_lookup(a.plan, coords[row], f >> 1);

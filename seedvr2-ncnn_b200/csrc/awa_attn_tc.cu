@@ -679,8 +679,9 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
     const uint32_t lane_base = (uint32_t)(ptid & ~31) << 16;
     const int kr = ptid & 63;    // K row of this thread
     const int khalf = ptid >> 6;  // ... and its half (features 64 khalf ..): warps 8-9 / 10-11
-    const int ppa = RD ? RD / 6 : a.plan.pairs_per_axis;
-    const int rope_dim = RD ? RD : a.plan.rope_dim;
+    // RD < 0: Q/K arrive rotated (by the producer's epilogue); nothing to rotate
+    const int ppa = RD > 0 ? RD / 6 : a.plan.pairs_per_axis;
+    const int rope_dim = RD > 0 ? RD : a.plan.rope_dim;
     const int bwc = a.plan.tc_bwc > 0 ? a.plan.tc_bwc : 1;
     const uint2* table = a.plan.rope_factors_bf16;  // read through L1
     volatile int* abort = &sh.abort;
@@ -699,7 +700,7 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
         if (!warp_all(wait_bar(&sh.bar.q_loaded, q_loaded_phase, abort, a.error_flag, 11)))
             return false;
         q_loaded_phase ^= 1;
-        if (PACKED)
+        if (PACKED || RD < 0)
             return true;
         const int hoff = job.win.h0 - job.win.h0n, woff = job.win.w0 - job.win.w0n;
 #pragma unroll 1
@@ -715,13 +716,15 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
             row_bases(base, valid, geo, a.plan.text_tokens, row_h, row_w, hoff, woff, ptid & 63, ppa);
             uint32_t words[32];
             load_half_row(words, tile, kQRows, ptid, 0);
-            rotate_half_row<0, RD>(words, base, table, ppa, rope_dim);
+            if constexpr (RD >= 0)
+                rotate_half_row<0, RD>(words, base, table, ppa, rope_dim);
 #pragma unroll
             for (int k = 0; k < 8; k++)
                 *reinterpret_cast<uint4*>(tile + swizzled_offset(kQRows, ptid, k)) =
                     make_uint4(words[4 * k], words[4 * k + 1], words[4 * k + 2], words[4 * k + 3]);
             load_half_row(words, tile, kQRows, ptid, 1);
-            rotate_half_row<1, RD>(words, base, table, ppa, rope_dim);
+            if constexpr (RD >= 0)
+                rotate_half_row<1, RD>(words, base, table, ppa, rope_dim);
 #pragma unroll
             for (int k = 0; k < 8; k++)
                 *reinterpret_cast<uint4*>(tile + swizzled_offset(kQRows, ptid, 8 + k)) =
@@ -776,7 +779,11 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
             const uint64_t mask = block_mask<PACKED>(a, job, geo);
             if (!warp_all(wait_bar(&sh.bar.kv_loaded[stage], use & 1, abort, a.error_flag, 13)))
                 return;
-            if (!PACKED)
+            if constexpr (!PACKED && RD < 0)
+            {
+                // K arrived rotated: the stage goes to the MMA as loaded
+            }
+            else if (!PACKED)
             {
                 // one row, half its features, per thread (same shape as the Q step)
                 uint8_t* k_tile = sh.kv[stage][0];
@@ -784,10 +791,13 @@ __device__ void rope_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_t t
                 row_bases(base, (mask >> kr) & 1ull, geo, a.plan.text_tokens, row_h, row_w, hoff, woff, kr, ppa);
                 uint32_t words[32];
                 load_half_row(words, k_tile, kKeys, kr, khalf);
-                if (khalf == 0)
-                    rotate_half_row<0, RD>(words, base, table, ppa, rope_dim);
-                else
-                    rotate_half_row<1, RD>(words, base, table, ppa, rope_dim);
+                if constexpr (RD >= 0)
+                {
+                    if (khalf == 0)
+                        rotate_half_row<0, RD>(words, base, table, ppa, rope_dim);
+                    else
+                        rotate_half_row<1, RD>(words, base, table, ppa, rope_dim);
+                }
 #pragma unroll
                 for (int k = 0; k < 8; k++)
                     *reinterpret_cast<uint4*>(k_tile + swizzled_offset(kKeys, kr, 8 * khalf + k)) =
@@ -1415,17 +1425,25 @@ int launch_attention_tc(const AttnArgs& args, int packed, int in_dtype, int out_
     const int64_t out_size = out_dtype == kF32 ? 4 : 2;
     a.out_v8 = (reinterpret_cast<uintptr_t>(args.out) % 32 == 0) && (args.out_token_stride * out_size) % 32 == 0 &&
                (reinterpret_cast<uintptr_t>(args.text_partial) % 32 == 0) && (args.heads * args.head_dim * 2) % 32 == 0;
-    ProfileScope prof(packed ? "awa_attention_tc_packed" : "awa_attention_tc_fused", stream);
+    ProfileScope prof(packed ? "awa_attention_tc_packed"
+                             : args.rotate ? "awa_attention_tc_fused" : "awa_attention_tc_prerotated",
+                      stream);
     // The packed path applies no RoPE; the fused path has a 126-wide (21 pairs per axis) instance.
     const bool rd126 = p.rope_dim == 126 && p.pairs_per_axis == 21;
+    // Q/K rotated by the producer: the instance without rotation (RD = -1)
+    const bool rotated = !packed && !args.rotate;
     if (out_dtype == kF32)
     {
         if (packed)
             return launch_tc<true, float, 0>(a, maps, stream);
+        if (rotated)
+            return launch_tc<false, float, -1>(a, maps, stream);
         return rd126 ? launch_tc<false, float, 126>(a, maps, stream) : launch_tc<false, float, 0>(a, maps, stream);
     }
     if (packed)
         return launch_tc<true, bf16, 0>(a, maps, stream);
+    if (rotated)
+        return launch_tc<false, bf16, -1>(a, maps, stream);
     return rd126 ? launch_tc<false, bf16, 126>(a, maps, stream) : launch_tc<false, bf16, 0>(a, maps, stream);
 }
 

@@ -97,6 +97,7 @@ struct AttnArgs
     int window_begin = 0;  // fused, sharded: first window of this launch
     int* error_flag = nullptr;
     int out_v8 = 0;  // tcgen05 kernel: output rows (and text partials) are 32-byte aligned
+    int rotate = 1;  // fused: 1 = rotate Q/K as they are loaded, 0 = they arrive rotated (awa_qkv_project_rotated)
 };
 
 // Launchers (return a cudaError_t value as int).
@@ -130,9 +131,13 @@ int launch_attention_tc(const AttnArgs& args, int packed, int in_dtype, int out_
 int launch_wait_selftest(uint64_t limit_ns, int* error_flag, int* observed, cudaStream_t stream);
 // x W^T with the per-head RMSNorm of Q and K (head_dim 128); arguments checked
 // by the caller.
+// rope_plan / rope_mode: 0 = no rotation; 1 = rows are the plan's video
+// tokens, 2 = its text tokens: Q and K heads are rotated (MMRoPE, fp32, with
+// each token's window-local coordinates) after the RMSNorm.
 int launch_qkv_project(int tokens, int model_dim, int heads, const void* x, int64_t x_stride, const void* w,
                        int64_t w_stride, const float* gamma_q, const float* gamma_k, float eps, int out_dtype,
-                       void* out, int64_t out_stride, cudaStream_t stream);
+                       void* out, int64_t out_stride, cudaStream_t stream, const PlanDevice* rope_plan = nullptr,
+                       int rope_mode = 0);
 // out = resid + bf16(x W^T + bias) * gate per output channel (n_out % 128 == 0);
 // arguments checked by the caller.
 int launch_out_project(int tokens, int k_dim, int n_out, const void* x, int64_t x_stride, const void* w,

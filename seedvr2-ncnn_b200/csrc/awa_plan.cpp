@@ -745,7 +745,7 @@ static int forward_impl(const awa_plan* cplan, int precision, int heads, int hea
                         int window_end, int in_dtype, const void* video_qkv, int64_t vts, int64_t vqs,
                         const void* text_qkv, int64_t tts, int64_t tqs, int out_dtype, void* video_out,
                         int64_t vots, void* workspace, size_t workspace_bytes, int* partial_dtype,
-                        cudaStream_t stream)
+                        cudaStream_t stream, int rotate = 1)
 {
     awa_plan* plan = const_cast<awa_plan*>(cplan);
     const int64_t head_row = (int64_t)heads * head_dim;
@@ -782,6 +782,7 @@ static int forward_impl(const awa_plan* cplan, int precision, int heads, int hea
     args.out_token_stride = vots;
     args.text_partial = static_cast<float*>(workspace);
     args.window_begin = window_begin;
+    args.rotate = rotate;
     int count = 0, rc = AWA_OK;
     const int2* items = range_items(plan, tc, window_begin, window_end, &count, &rc);
     if (rc)
@@ -789,11 +790,41 @@ static int forward_impl(const awa_plan* cplan, int precision, int heads, int hea
     return run_attention(plan, precision, args, 0, in_dtype, out_dtype, items, count, stream);
 }
 
+static int forward_whole(const awa_plan* plan, int precision, int heads, int head_dim, int in_dtype,
+                         const void* video_qkv, int64_t video_token_stride, int64_t video_qkv_stride,
+                         const void* text_qkv, int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype,
+                         void* video_out, int64_t video_token_stride_out, void* text_out,
+                         int64_t text_token_stride_out, void* workspace, size_t workspace_bytes, awa_stream_t stream,
+                         int rotate);
+
 int awa_forward(const awa_plan* plan, int precision, int heads, int head_dim, int in_dtype, const void* video_qkv,
                 int64_t video_token_stride, int64_t video_qkv_stride, const void* text_qkv,
                 int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype, void* video_out,
                 int64_t video_token_stride_out, void* text_out, int64_t text_token_stride_out, void* workspace,
                 size_t workspace_bytes, awa_stream_t stream)
+{
+    return forward_whole(plan, precision, heads, head_dim, in_dtype, video_qkv, video_token_stride, video_qkv_stride,
+                         text_qkv, text_token_stride, text_qkv_stride, out_dtype, video_out, video_token_stride_out,
+                         text_out, text_token_stride_out, workspace, workspace_bytes, stream, 1);
+}
+
+int awa_forward_prerotated(const awa_plan* plan, int precision, int heads, int head_dim, int in_dtype,
+                           const void* video_qkv, int64_t video_token_stride, int64_t video_qkv_stride,
+                           const void* text_qkv, int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype,
+                           void* video_out, int64_t video_token_stride_out, void* text_out,
+                           int64_t text_token_stride_out, void* workspace, size_t workspace_bytes, awa_stream_t stream)
+{
+    return forward_whole(plan, precision, heads, head_dim, in_dtype, video_qkv, video_token_stride, video_qkv_stride,
+                         text_qkv, text_token_stride, text_qkv_stride, out_dtype, video_out, video_token_stride_out,
+                         text_out, text_token_stride_out, workspace, workspace_bytes, stream, 0);
+}
+
+static int forward_whole(const awa_plan* plan, int precision, int heads, int head_dim, int in_dtype,
+                         const void* video_qkv, int64_t video_token_stride, int64_t video_qkv_stride,
+                         const void* text_qkv, int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype,
+                         void* video_out, int64_t video_token_stride_out, void* text_out,
+                         int64_t text_token_stride_out, void* workspace, size_t workspace_bytes, awa_stream_t stream,
+                         int rotate)
 {
     int rc = check_heads(plan, heads, head_dim);
     if (rc)
@@ -803,7 +834,7 @@ int awa_forward(const awa_plan* plan, int precision, int heads, int head_dim, in
     int partial_dtype = AWA_F32;
     rc = forward_impl(plan, precision, heads, head_dim, 0, plan->info.window_count, in_dtype, video_qkv,
                       video_token_stride, video_qkv_stride, text_qkv, text_token_stride, text_qkv_stride, out_dtype,
-                      video_out, video_token_stride_out, workspace, workspace_bytes, &partial_dtype, stream);
+                      video_out, video_token_stride_out, workspace, workspace_bytes, &partial_dtype, stream, rotate);
     if (rc)
         return rc;
     return launch_status(awa::launch_text_reduce(plan->dev, heads, head_dim, 0, partial_dtype, workspace,
@@ -917,6 +948,41 @@ int awa_qkv_project(int tokens, int model_dim, int heads, int head_dim, const vo
     return launch_status(awa::launch_qkv_project(tokens, model_dim, heads, x, x_stride, w, w_stride, gamma_q, gamma_k,
                                                  eps, out_dtype, out, out_stride, static_cast<cudaStream_t>(stream)),
                          "awa_qkv_project launch");
+}
+
+int awa_qkv_project_rotated(int tokens, int model_dim, int heads, int head_dim, const void* x, int64_t x_stride,
+                            const void* w, int64_t w_stride, const float* gamma_q, const float* gamma_k, float eps,
+                            const awa_plan* plan, int branch, int out_dtype, void* out, int64_t out_stride,
+                            awa_stream_t stream)
+{
+    int rc = check_heads(plan, heads, head_dim);
+    if (rc)
+        return rc;
+    if (branch != AWA_BRANCH_VIDEO && branch != AWA_BRANCH_TEXT)
+        return fail(AWA_ERR_INVALID, "awa_qkv_project_rotated: branch must be AWA_BRANCH_VIDEO or AWA_BRANCH_TEXT");
+    const int rows = branch == AWA_BRANCH_VIDEO ? plan->info.source_tokens : plan->info.text_tokens;
+    if (tokens != rows)
+        return fail(AWA_ERR_INVALID, "awa_qkv_project_rotated: %d tokens, the plan's %s branch has %d", tokens,
+                    branch == AWA_BRANCH_VIDEO ? "video" : "text", rows);
+    if (head_dim < plan->info.rope_dim)
+        return fail(AWA_ERR_INVALID, "awa_qkv_project_rotated: head_dim %d < rope_dim %d", head_dim,
+                    plan->info.rope_dim);
+    if (head_dim != 128)
+        return fail(AWA_ERR_INVALID, "awa_qkv_project_rotated: head_dim %d (the tensor-core kernel needs 128)",
+                    head_dim);
+    const int64_t n_out = 3 * (int64_t)heads * head_dim;
+    if (model_dim <= 0 || n_out > 0x7fffffff || !x || !w || !gamma_q || !gamma_k || !out || !valid_dtype(out_dtype) ||
+        x_stride < model_dim || w_stride < model_dim || out_stride < n_out || !(eps >= 0.f))
+        return fail(AWA_ERR_INVALID, "awa_qkv_project_rotated: invalid sizes, dtype, eps or NULL tensor");
+    const size_t osz = dtype_size(out_dtype);
+    if (!is_aligned16(x) || !is_aligned16(w) || (x_stride * 2) % 16 || (w_stride * 2) % 16 ||
+        reinterpret_cast<uintptr_t>(out) % 32 || (out_stride * (int64_t)osz) % 32)
+        return fail(AWA_ERR_INVALID,
+                    "awa_qkv_project_rotated: x and w need 16-byte aligned rows, out 32-byte aligned rows");
+    return launch_status(awa::launch_qkv_project(tokens, model_dim, heads, x, x_stride, w, w_stride, gamma_q, gamma_k,
+                                                 eps, out_dtype, out, out_stride, static_cast<cudaStream_t>(stream),
+                                                 &plan->dev, branch == AWA_BRANCH_VIDEO ? 1 : 2),
+                         "awa_qkv_project_rotated launch");
 }
 
 int awa_out_project(int tokens, int in_dim, int out_dim, const void* x, int64_t x_stride, const void* w,

@@ -29,6 +29,7 @@
 // Every wait is bounded; a wait that gives up sets an abort flag that stops
 // the other roles and reports through the device error flag.
 #include "awa_internal.h"
+#include "awa_rows.cuh"
 #include "tcgen05.cuh"
 
 #include <cuda.h>
@@ -77,6 +78,10 @@ struct ProjArgs
     int64_t out_stride;  // elements
     int out_f32;
     int* error_flag;
+    // kQkv, rotated output: 0 = none, 1 = video rows (coordinates through the
+    // plan's video_positions / position_coords), 2 = text rows (i, i, i)
+    int rope_mode;
+    PlanDevice rope;
 };
 
 struct ProjMaps
@@ -386,11 +391,19 @@ __device__ void epilogue_qkv(const ProjArgs& p, ProjShared& sh, uint32_t tmem)
     for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, i++)
     {
         const int buf = i & 1;
+        const int token = (t / p.tiles_n) * kTileM + row;
+        const int n0 = (t % p.tiles_n) * kTileN;
+        // this row's RoPE coordinates (window-local t + text count, h, w for a
+        // video token, (i, i, i) for text token i; awa_layers.cpp:896-908),
+        // fetched before the wait for the accumulator
+        short4 coords = make_short4(0, 0, 0, 0);
+        if (p.rope_mode == 1 && token < p.tokens)
+            coords = reinterpret_cast<const short4*>(p.rope.position_coords)[__ldg(p.rope.video_positions + token)];
+        else if (p.rope_mode == 2)
+            coords = make_short4((short)token, (short)token, (short)token, 0);
         if (!warp_all(wait_bar(&sh.acc_full[buf], (i >> 1) & 1, abort, p.error_flag, 66)))
             return;
         tc::fence_after_sync();
-        const int token = (t / p.tiles_n) * kTileM + row;
-        const int n0 = (t % p.tiles_n) * kTileN;
 #pragma unroll 1
         for (int h = 0; h < 2; h++)
         {
@@ -423,6 +436,25 @@ __device__ void epilogue_qkv(const ProjArgs& p, ProjShared& sh, uint32_t tmem)
 #pragma unroll
                 for (int k = 0; k < 128; k++)
                     v[k] = v[k] * coef * __ldg(gamma + k);
+                if (p.rope_mode)
+                {
+                    // MMRoPE in fp32 on the normalised head, as the reference's
+                    // fp32 layer (awa_layers.cpp:937-950): pair j of the first
+                    // rope_dim features, axis t / h / w by pairs_per_axis
+                    const int ppa = p.rope.pairs_per_axis;
+#pragma unroll
+                    for (int j = 0; j < 64; j++)
+                    {
+                        const int axis = j >= 2 * ppa ? 2 : j >= ppa ? 1 : 0;
+                        const int coord = axis == 0 ? coords.x : axis == 1 ? coords.y : coords.z;
+                        const bool on = 2 * j < p.rope.rope_dim;
+                        const float2 cs = __ldg(p.rope.rope_table + (on ? coord * ppa + j - axis * ppa : 0));
+                        float o0, o1;
+                        rope_rotate(v[2 * j], v[2 * j + 1], cs.x, cs.y, o0, o1);
+                        v[2 * j] = on ? o0 : v[2 * j];
+                        v[2 * j + 1] = on ? o1 : v[2 * j + 1];
+                    }
+                }
             }
             char* dst = static_cast<char*>(p.out) + ((int64_t)token * p.out_stride + f0) * (p.out_f32 ? 4 : 2);
             if (p.out_f32)
@@ -562,7 +594,8 @@ int sm_count_proj()
 
 int launch_qkv_project(int tokens, int model_dim, int heads, const void* x, int64_t x_stride, const void* w,
                        int64_t w_stride, const float* gamma_q, const float* gamma_k, float eps, int out_dtype,
-                       void* out, int64_t out_stride, cudaStream_t stream)
+                       void* out, int64_t out_stride, cudaStream_t stream, const PlanDevice* rope_plan,
+                       int rope_mode)
 {
     const int n_out = 3 * heads * 128;
     ProjMaps maps;
@@ -589,12 +622,15 @@ int launch_qkv_project(int tokens, int model_dim, int heads, const void* x, int6
     p.out_stride = out_stride;
     p.out_f32 = out_dtype == kF32;
     p.error_flag = device_error_flag();
+    p.rope_mode = rope_plan ? rope_mode : 0;
+    if (rope_plan)
+        p.rope = *rope_plan;
     const size_t smem = sizeof(ProjShared) + 1024;
     cudaError_t err =
         cudaFuncSetAttribute(qkv_proj_kernel<kQkv>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess)
         return (int)err;
-    ProfileScope prof("awa_qkv_project", stream);
+    ProfileScope prof(p.rope_mode ? "awa_qkv_project_rotated" : "awa_qkv_project", stream);
     const int grid = p.tiles < sm_count_proj() ? p.tiles : sm_count_proj();
     qkv_proj_kernel<kQkv><<<grid, kThreads, smem, stream>>>(p, maps);
     return (int)cudaGetLastError();
@@ -618,6 +654,7 @@ int launch_out_project(int tokens, int k_dim, int n_out, const void* x, int64_t 
     p.k_steps = (k_dim + kTileK - 1) / kTileK;
     p.gamma_q = p.gamma_k = nullptr;
     p.eps = 0.f;
+    p.rope_mode = 0;
     p.bias = bias;
     p.gate = gate;
     p.resid = resid;
