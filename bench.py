@@ -54,7 +54,12 @@ WORKLOADS = {
     "cfg5": ((9, 45, 80), (3, 6, 10), 0, "bf16", "33x720x1280 video -> 9x45x80 grid, adaptive 3x8x8 windows"),
     "cfg5-fp32": ((9, 45, 80), (3, 6, 10), 0, "fp32", "9x45x80 grid, adaptive 3x8x8 windows, fp32 block"),
     "cfg2": ((6, 16, 16), (2, 8, 8), 0, "bf16", "21x256x256 video -> 6x16x16 grid, 3x8x8 windows"),
+    "cfg4b": ((21, 64, 64), (21, 8, 8), 0, "bf16", "21x64x64 grid, 1x8x8 windows (num_windows 21,8,8): 1344 windows"),
+    "cfg4-f32qkv": ((21, 64, 64), (6, 8, 8), 0, "bf16",
+                    "cfg4 fed fp32 QKV in a bf16 block (the reference's promoted fp32 QKV): converted to bf16 "
+                    "in the workspace, then the tensor-core kernel"),
 }
+INPUT_F32 = {"cfg4-f32qkv"}  # workloads whose QKV rows are fp32 although the block is bf16
 
 
 def window_costs(grid, num, shifted):
@@ -83,7 +88,7 @@ def workload_config(name, world, mode="replicas"):
     """The `config` both arms print for a workload (identical keys and values)."""
     grid, num, shifted, precision, desc = WORKLOADS[name]
     n_v = grid[0] * grid[1] * grid[2]
-    esize = 2 if precision == "bf16" else 4
+    esize = 2 if precision == "bf16" and name not in INPUT_F32 else 4
     in_bytes = (n_v + TEXT) * 3 * HEADS * HEAD_DIM * esize
     parallelism = (f"sharded: one layer's windows split over {world} GPU(s), NCCL text all-reduce + video all-gather"
                    if mode == "sharded" else f"replicas: {world} independent layer(s), one per GPU")
@@ -451,20 +456,22 @@ def run_b200(args, rank, world, local_rank):
     grid, num, shifted, precision, desc = WORKLOADS[name]
     prec = awa_b200.AWA_PREC_BF16 if precision == "bf16" else awa_b200.AWA_PREC_FP32
     dtype = torch.bfloat16 if precision == "bf16" else torch.float32
+    in_dtype = torch.float32 if name in INPUT_F32 else dtype
     esize = 2 if precision == "bf16" else 4
+    in_esize = 4 if in_dtype == torch.float32 else 2
     wins, lengths = window_costs(grid, num, shifted)
     W = len(lengths)
     flops = attention_flops(lengths)
     n_v = grid[0] * grid[1] * grid[2]
     plan = awa_b200.AwaPlan(*grid, *num, text_tokens=TEXT, shifted=bool(shifted))
-    kernel_kind = plan.attention_kernel_kind(prec, HEADS, HEAD_DIM, dtype)
+    kernel_kind = plan.attention_kernel_kind(prec, HEADS, HEAD_DIM, in_dtype)
 
     gen = torch.Generator(device=device).manual_seed(1234 + rank)
-    video_qkv = torch.randn(n_v, 3, HEADS, HEAD_DIM, device=device, generator=gen).to(dtype)
-    text_qkv = torch.randn(TEXT, 3, HEADS, HEAD_DIM, device=device, generator=gen).to(dtype)
+    video_qkv = torch.randn(n_v, 3, HEADS, HEAD_DIM, device=device, generator=gen).to(in_dtype)
+    text_qkv = torch.randn(TEXT, 3, HEADS, HEAD_DIM, device=device, generator=gen).to(in_dtype)
     video_out = torch.empty(n_v, HEADS, HEAD_DIM, device=device, dtype=dtype)
     text_out = torch.empty(TEXT, HEADS, HEAD_DIM, device=device, dtype=dtype)
-    workspace = torch.empty(plan.workspace_bytes(HEADS, HEAD_DIM), device=device, dtype=torch.uint8)
+    workspace = torch.empty(plan.workspace_bytes(HEADS, HEAD_DIM, prec, in_dtype), device=device, dtype=torch.uint8)
     stream = torch.cuda.current_stream(device)
 
     def step():
@@ -510,8 +517,8 @@ def run_b200(args, rank, world, local_rank):
     e2e_ms, e2e_steps = None, 0
     if not args.no_e2e:
         e2e_steps = max(3, min(args.steps, args.e2e_steps))
-        host_v = torch.empty(video_qkv.shape, dtype=dtype, pin_memory=True)
-        host_t = torch.empty(text_qkv.shape, dtype=dtype, pin_memory=True)
+        host_v = torch.empty(video_qkv.shape, dtype=video_qkv.dtype, pin_memory=True)
+        host_t = torch.empty(text_qkv.shape, dtype=text_qkv.dtype, pin_memory=True)
         host_v.copy_(video_qkv)
         host_t.copy_(text_qkv)
         out_v = torch.empty(video_out.shape, dtype=dtype, pin_memory=True)
@@ -588,9 +595,10 @@ def run_b200(args, rank, world, local_rank):
     peak_src = "measured" if hbm_peak else "fallback"
     hbm_peak = hbm_peak or 6650.0
     tensor_peak = tensor_peak or 1590.0
-    in_bytes = (n_v + TEXT) * 3 * HEADS * HEAD_DIM * esize
+    in_bytes = (n_v + TEXT) * 3 * HEADS * HEAD_DIM * in_esize
     out_bytes = (n_v + TEXT) * HEADS * HEAD_DIM * esize
-    alg_bytes = in_bytes + out_bytes  # read the source QKV once, write the outputs once
+    # the attention kernel reads bf16 rows (for fp32 inputs: the converted copy)
+    alg_bytes = (n_v + TEXT) * 3 * HEADS * HEAD_DIM * (2 if kernel_kind == 1 else esize) + out_bytes
     achieved_gbs = alg_bytes / (attn_ms / 1000.0) / 1e9
     achieved_tflops = flops / (attn_ms / 1000.0) / 1e12
     traffic = recorded_traffic(f"{name}:{attn_name}")

@@ -148,6 +148,11 @@ int awa_unpack(const awa_plan* plan, int heads, int head_dim, int in_dtype, cons
  * no packed intermediate is written. Needs a workspace of
  * awa_forward_workspace_bytes(). Outputs equal the four-layer chain's. */
 size_t awa_forward_workspace_bytes(const awa_plan* plan, int heads, int head_dim);
+/* The workspace awa_forward needs for these precision and input dtype: the
+ * above, plus, for fp32 QKV rows on the tensor-core path (AWA_PREC_BF16, a bf16
+ * block fed the reference's promoted fp32 QKV, dit_precision.cpp:314-315), a
+ * bf16 copy of the rows that one pass converts before the attention. */
+size_t awa_forward_workspace_bytes_for(const awa_plan* plan, int precision, int in_dtype, int heads, int head_dim);
 int awa_forward(const awa_plan* plan, int precision, int heads, int head_dim, int in_dtype, const void* video_qkv,
                 int64_t video_token_stride, int64_t video_qkv_stride, const void* text_qkv,
                 int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype, void* video_out,
@@ -361,10 +366,12 @@ int awa_device_status(void);
  * usable. */
 int awa_selftest_bounded_wait(unsigned limit_us, int* observed, awa_stream_t stream);
 
-/* Which attention kernel awa_window_attention / awa_forward would launch for
- * these arguments: 1 = tcgen05 (sm_100a tensor cores: AWA_PREC_BF16 with bf16
- * inputs and head_dim 128), 2 = fp32 SIMT (everything else; fp32 inputs at
- * AWA_PREC_BF16 are computed in fp32, which is within the bf16 tolerance). */
+/* Which attention kernel awa_forward would launch for these arguments:
+ * 1 = tcgen05 (sm_100a tensor cores: AWA_PREC_BF16 with head_dim 128; fp32
+ * QKV rows are first converted to bf16 in the workspace, see
+ * awa_forward_workspace_bytes_for), 2 = fp32 SIMT (AWA_PREC_FP32, other head
+ * sizes). awa_window_attention (packed rows) takes the tensor cores for bf16
+ * packed rows only. */
 int awa_attention_kernel_kind(const awa_plan* plan, int precision, int in_dtype, int heads, int head_dim);
 
 /* Opt-in launch profiler (the counterpart of the reference's

@@ -39,6 +39,7 @@ AWA_BRANCH_TEXT = 1
 EXPORTED_SYMBOLS = (
     "awa_make_windows", "awa_plan_create", "awa_plan_create_host", "awa_plan_destroy", "awa_plan_get_info", "awa_plan_get_maps",
     "awa_pack", "awa_mmrope", "awa_window_attention", "awa_unpack", "awa_forward_workspace_bytes", "awa_forward",
+    "awa_forward_workspace_bytes_for",
     "awa_forward_noalloc", "awa_forward_prerotated", "awa_qkv_project_rotated",
     "awa_forward_windows", "awa_text_finalize", "awa_scatter_video_shard", "awa_gather_video_shard",
     "awa_window_range_video_rows", "awa_partition_windows", "awa_qkv_project", "awa_out_project", "awa_device_status",
@@ -124,6 +125,7 @@ def library() -> ctypes.CDLL:
         "awa_window_attention": (i, [p, i, i, i, i, p, i64, i, p, i64, p]),
         "awa_unpack": (i, [p, i, i, i, p, i64, i, p, i64, p, i64, p]),
         "awa_forward_workspace_bytes": (sz, [p, i, i]),
+        "awa_forward_workspace_bytes_for": (sz, [p, i, i, i, i]),
         "awa_forward": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p, sz, p]),
         "awa_forward_noalloc": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p]),
         "awa_forward_prerotated": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p, sz, p]),
@@ -342,8 +344,13 @@ class AwaPlan:
         return video, text
 
     # ---------------------------------------------------------------- fused chain
-    def workspace_bytes(self, heads: int, head_dim: int) -> int:
-        return int(library().awa_forward_workspace_bytes(self._handle, heads, head_dim))
+    def workspace_bytes(self, heads: int, head_dim: int, precision=None, in_dtype=None) -> int:
+        """awa_forward's workspace; with precision and in_dtype (a torch dtype)
+        it includes the bf16 copy that fp32 rows on the tensor-core path need."""
+        if precision is None:
+            return int(library().awa_forward_workspace_bytes(self._handle, heads, head_dim))
+        return int(library().awa_forward_workspace_bytes_for(self._handle, precision, _dtype_code_of(in_dtype),
+                                                             heads, head_dim))
 
     def forward(self, video_qkv, text_qkv, precision=AWA_PREC_BF16, out_dtype=None, workspace=None,
                 video_out=None, text_out=None, stream=None):
@@ -355,7 +362,7 @@ class AwaPlan:
             video_out = torch.empty(self.info.source_tokens, heads, hd, dtype=dt, device=video_qkv.device)
         if text_out is None:
             text_out = torch.empty(self.info.text_tokens, heads, hd, dtype=dt, device=video_qkv.device)
-        need = self.workspace_bytes(heads, hd)
+        need = self.workspace_bytes(heads, hd, precision, video_qkv.dtype)
         if workspace is None:
             workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=video_qkv.device)
         vts, vqs = _qkv_strides(video_qkv)
@@ -378,8 +385,8 @@ class AwaPlan:
         if text_out is None:
             text_out = torch.empty(self.info.text_tokens, heads, hd, dtype=dt, device=video_qkv.device)
         if workspace is None:
-            workspace = torch.empty(max(self.workspace_bytes(heads, hd), 16), dtype=torch.uint8,
-                                    device=video_qkv.device)
+            workspace = torch.empty(max(self.workspace_bytes(heads, hd, precision, video_qkv.dtype), 16),
+                                    dtype=torch.uint8, device=video_qkv.device)
         vts, vqs = _qkv_strides(video_qkv)
         tts, tqs = _qkv_strides(text_qkv)
         _check(library().awa_forward_prerotated(self._handle, precision, heads, hd, _dtype_code(video_qkv),

@@ -400,6 +400,42 @@ __global__ void __launch_bounds__(32 * kShardRowsPerBlock)
         to[i] = from[i];
 }
 
+// fp32 QKV rows -> dense bf16 rows: a warp per token, 8 elements (32 bytes
+// in, 16 out) per lane step; float4 loads when the rows are 16-byte aligned.
+template <bool VEC>
+__global__ void __launch_bounds__(256) rows_to_bf16_kernel(const float* __restrict__ src, int64_t ts, int64_t qs,
+                                                           int tokens, int row, uint4* __restrict__ dst)
+{
+    const int chunks = row / 8;  // per q/k/v segment
+    for (int t = blockIdx.x * 8 + (threadIdx.x >> 5); t < tokens; t += gridDim.x * 8)
+        for (int c = threadIdx.x & 31; c < 3 * chunks; c += 32)
+        {
+            const int q = c / chunks, e = 8 * (c - q * chunks);
+            const float* p = src + t * ts + q * qs + e;
+            float v[8];
+            if (VEC)
+            {
+                const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+                const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+                v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+            }
+            else
+            {
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    v[k] = __ldg(p + k);
+            }
+            uint32_t w[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+            {
+                const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+                w[k] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+            dst[(int64_t)t * 3 * chunks + c] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+}
+
 template <template <typename, typename> class Fn, typename... Args>
 int dispatch2(int in_dtype, int out_dtype, Args&&... args)
 {
@@ -604,6 +640,23 @@ int launch_text_scale(int rows, int heads, int head_dim, const float* text_sum, 
     else
         text_scale<bf16><<<grid, threads, 0, stream>>>(rows, head_row, text_sum, divisor, (bf16*)text_out,
                                                        text_token_stride);
+    return (int)cudaGetLastError();
+}
+
+int launch_rows_to_bf16(const void* src, int64_t ts, int64_t qs, int tokens, int64_t row, void* dst,
+                        cudaStream_t stream)
+{
+    if (tokens <= 0)
+        return 0;
+    if (row % 8 || row > (1 << 24) || reinterpret_cast<uintptr_t>(dst) % 16)
+        return (int)cudaErrorInvalidValue;
+    ProfileScope prof("awa_rows_to_bf16", stream);
+    const bool vec = reinterpret_cast<uintptr_t>(src) % 16 == 0 && ts % 4 == 0 && qs % 4 == 0;
+    const int grid = (int)std::min<int64_t>((tokens + 7) / 8, 148 * 16);
+    if (vec)
+        rows_to_bf16_kernel<true><<<grid, 256, 0, stream>>>((const float*)src, ts, qs, tokens, (int)row, (uint4*)dst);
+    else
+        rows_to_bf16_kernel<false><<<grid, 256, 0, stream>>>((const float*)src, ts, qs, tokens, (int)row, (uint4*)dst);
     return (int)cudaGetLastError();
 }
 

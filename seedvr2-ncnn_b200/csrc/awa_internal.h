@@ -120,6 +120,10 @@ int launch_text_reduce(const PlanDevice& plan, int heads, int head_dim, int pack
                        void* text_out, int64_t text_token_stride, cudaStream_t stream);
 int launch_text_scale(int rows, int heads, int head_dim, const float* text_sum, float divisor, int out_dtype,
                       void* text_out, int64_t text_token_stride, cudaStream_t stream);
+// fp32 QKV rows (token stride ts, q/k/v stride qs, `row` = H * d elements,
+// a multiple of 8) -> dense bf16 rows [tokens][3][row], round to nearest even.
+int launch_rows_to_bf16(const void* src, int64_t ts, int64_t qs, int tokens, int64_t row, void* dst,
+                        cudaStream_t stream);
 int launch_shard_copy(const PlanDevice& plan, int heads, int head_dim, int window_begin, int window_end, int dtype,
                       const void* src, int64_t src_stride, void* dst, int64_t dst_stride, int to_source,
                       cudaStream_t stream);

@@ -615,10 +615,28 @@ int awa_mmrope(const awa_plan* plan, int heads, int head_dim, int in_dtype, cons
                          "awa_mmrope launch");
 }
 
+// The tcgen05 kernel serves bf16 blocks with head_dim 128 on plans whose
+// windows it can fetch as boxes. It reads bf16 rows; the fused forward
+// converts fp32 QKV rows to bf16 into its workspace first.
+static bool tc_capable(const awa_plan* plan, int precision, int head_dim)
+{
+    return plan && precision == AWA_PREC_BF16 && head_dim == 128 && plan->tc_slabs;
+}
+
 int awa_attention_kernel_kind(const awa_plan* plan, int precision, int in_dtype, int heads, int head_dim)
 {
     (void)heads;
-    return plan && precision == AWA_PREC_BF16 && in_dtype == AWA_BF16 && head_dim == 128 && plan->tc_slabs ? 1 : 2;
+    (void)in_dtype;
+    return tc_capable(plan, precision, head_dim) ? 1 : 2;
+}
+
+// Bytes of the bf16 copy of the QKV rows that the fused forward makes for
+// fp32 rows on the tensor-core path (video then text, 256-byte aligned).
+static size_t conversion_bytes(const awa_plan* plan, int heads, int head_dim)
+{
+    const size_t row = 3 * (size_t)heads * head_dim * 2;
+    auto a256 = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    return a256((size_t)plan->info.source_tokens * row) + a256((size_t)plan->info.text_tokens * row);
 }
 
 static int run_attention(const awa_plan* plan, int precision, awa::AttnArgs& args, int packed, int in_dtype,
@@ -631,7 +649,7 @@ static int run_attention(const awa_plan* plan, int precision, awa::AttnArgs& arg
     args.item_count = item_count;
     if (item_count == 0)
         return AWA_OK;
-    if (awa_attention_kernel_kind(plan, precision, in_dtype, args.heads, args.head_dim) == 1)
+    if (tc_capable(plan, precision, args.head_dim) && in_dtype == AWA_BF16)
         return launch_status(awa::launch_attention_tc(args, packed, in_dtype, out_dtype, stream), "tcgen05 attention");
     return launch_status(awa::launch_attention_simt(args, packed, in_dtype, out_dtype, stream), "simt attention");
 }
@@ -660,7 +678,7 @@ int awa_window_attention(const awa_plan* plan, int precision, int heads, int hea
     args.qkv_token_stride = in_token_stride;
     args.out = attended;
     args.out_token_stride = out_token_stride;
-    const bool tc = awa_attention_kernel_kind(plan, precision, in_dtype, heads, head_dim) == 1;
+    const bool tc = tc_capable(plan, precision, head_dim) && in_dtype == AWA_BF16;  // packed rows: bf16 only
     if (tc && (!is_aligned16(packed) || !is_aligned16(attended) || (in_token_stride * dtype_size(in_dtype)) % 16 ||
                (out_token_stride * dtype_size(out_dtype)) % 16))
         return fail(AWA_ERR_INVALID, "awa_window_attention: bf16 tensor-core path needs 16-byte aligned rows");
@@ -697,6 +715,14 @@ size_t awa_forward_workspace_bytes(const awa_plan* plan, int heads, int head_dim
     if (!plan || heads <= 0 || head_dim <= 0)
         return 0;
     return (size_t)plan->info.window_count * plan->info.text_tokens * heads * head_dim * sizeof(float);
+}
+
+size_t awa_forward_workspace_bytes_for(const awa_plan* plan, int precision, int in_dtype, int heads, int head_dim)
+{
+    const size_t base = awa_forward_workspace_bytes(plan, heads, head_dim);
+    if (base == 0 || !(tc_capable(plan, precision, head_dim) && in_dtype == AWA_F32))
+        return base;
+    return ((base + 255) & ~(size_t)255) + conversion_bytes(plan, heads, head_dim);
 }
 
 // Items of windows [begin, end) in work order; cached per range on the device.
@@ -759,8 +785,37 @@ static int forward_impl(const awa_plan* cplan, int precision, int heads, int hea
     const size_t need = (size_t)(window_end - window_begin) * plan->info.text_tokens * head_row * sizeof(float);
     if (!workspace || workspace_bytes < need)
         return fail(AWA_ERR_INVALID, "awa_forward: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
-    const bool tc = awa_attention_kernel_kind(plan, precision, in_dtype, heads, head_dim) == 1;
+    const bool tc = tc_capable(plan, precision, head_dim);
     *partial_dtype = tc ? AWA_BF16 : AWA_F32;
+    if (tc && in_dtype == AWA_F32)
+    {
+        // fp32 rows (a bf16 block fed the reference's promoted fp32 QKV,
+        // dit_precision.cpp:314-315): one pass converts them to dense bf16 rows
+        // in the workspace behind the text partials; the kernel reads those.
+        const size_t at = (need + 255) & ~(size_t)255;
+        const size_t total = at + conversion_bytes(plan, heads, head_dim);
+        if (workspace_bytes < total)
+            return fail(AWA_ERR_INVALID,
+                        "awa_forward: fp32 QKV on the tensor-core path needs a workspace of %zu bytes "
+                        "(awa_forward_workspace_bytes_for), %zu given",
+                        total, workspace_bytes);
+        unsigned char* vdst = static_cast<unsigned char*>(workspace) + at;
+        unsigned char* tdst = vdst + (((size_t)plan->info.source_tokens * 3 * head_row * 2 + 255) & ~(size_t)255);
+        int rc = launch_status(awa::launch_rows_to_bf16(video_qkv, vts, vqs, plan->info.source_tokens, head_row, vdst,
+                                                        stream),
+                               "awa_forward fp32 -> bf16 rows (video)");
+        if (rc == AWA_OK)
+            rc = launch_status(awa::launch_rows_to_bf16(text_qkv, tts, tqs, plan->info.text_tokens, head_row, tdst,
+                                                        stream),
+                               "awa_forward fp32 -> bf16 rows (text)");
+        if (rc)
+            return rc;
+        video_qkv = vdst;
+        text_qkv = tdst;
+        vts = tts = 3 * head_row;
+        vqs = tqs = head_row;
+        in_dtype = AWA_BF16;
+    }
     if (tc)
     {
         const size_t in_size = dtype_size(in_dtype), out_size = dtype_size(out_dtype);

@@ -170,3 +170,33 @@ def test_invalid_arguments_rejected():
     # rope_dim > head_dim (awa_layers.cpp:920)
     assert lib.awa_mmrope(plan.handle, 2, 64, 0, 16, 384, 0, 16, 384, None) == -1
     awa_b200.device_status()
+
+
+@pytest.mark.parametrize("cfg", [CASES[3], CASES[4], CASES[6], CASES[11]], ids=case_id)
+def test_fp32_qkv_in_a_bf16_block_takes_the_tensor_cores(cfg, results):
+    """A bf16 block fed fp32 QKV (the reference promotes QKV to fp32 ahead of
+    Pack in its bf16 blocks, dit_precision.cpp:314-315): the fused forward
+    converts the rows to bf16 in its workspace (one rounding, to nearest
+    even) and runs the tcgen05 kernel -- the same result as handing it the
+    bf16 rows, within the bf16 tolerance of the oracle on the fp32 rows."""
+    v, t, ref = results(cfg, False)
+    plan = plan_for(cfg)
+    assert plan.attention_kernel_kind(AWA_PREC_BF16, cfg.heads, cfg.head_dim, torch.float32) == 1
+    need = plan.workspace_bytes(cfg.heads, cfg.head_dim, AWA_PREC_BF16, torch.float32)
+    assert need > plan.workspace_bytes(cfg.heads, cfg.head_dim)
+    dv, dt = to_device(v, torch.float32), to_device(t, torch.float32)
+    awa_b200.profile_reset()
+    awa_b200.profile_enable(True)
+    video, text = plan.forward(dv, dt, AWA_PREC_BF16, out_dtype=torch.float32)
+    awa_b200.profile_enable(False)
+    prof = awa_b200.profile_collect()
+    assert "awa_attention_tc_fused" in prof and "awa_rows_to_bf16" in prof, prof
+    video_b, text_b = plan.forward(dv.bfloat16(), dt.bfloat16(), AWA_PREC_BF16, out_dtype=torch.float32)
+    assert torch.equal(video, video_b) and torch.equal(text, text_b)
+    assert rel_l2(to_host(video), ref["video"]) < BF16_REL_L2
+    assert rel_l2(to_host(text), ref["text"]) < BF16_REL_L2
+    # a workspace that only holds the text partials is refused, not silently slower
+    small = torch.empty(plan.workspace_bytes(cfg.heads, cfg.head_dim), dtype=torch.uint8, device="cuda")
+    with pytest.raises(awa_b200.AwaError, match="awa_forward_workspace_bytes_for"):
+        plan.forward(dv, dt, AWA_PREC_BF16, workspace=small)
+    awa_b200.device_status()
