@@ -244,16 +244,22 @@ int awa_partition_windows(const awa_plan* plan, int parts, int* bounds);
  * Windows are independent (SeedVR2WindowAttention::forward,
  * awa_layers.cpp:1062-1120); the only coupling is the text mean
  * text += packed / window_count (SeedVR2AWAUnpack::forward :684-685). Each rank
- * computes a share of the layer and NCCL finishes it, so every rank ends with
- * the full outputs the ncnn boundary hands on:
- *   - window split: contiguous window ranges of near-equal attention cost
- *     (awa_partition_windows); the ranks' video rows are all-gathered and
- *     scattered to source order, the fp32 text partial sums all-reduced;
- *   - head split, when there are fewer than 4 windows per rank: each rank runs
- *     every window for a range of heads; the head slices of the video and text
- *     outputs are all-gathered.
- * No kernel reads a peer's memory; NCCL moves the data. libnccl.so.2 is
- * loaded on first use (inside a PyTorch process: the NCCL torch loaded). */
+ * computes a share of the layer and the ranks exchange the rest, so every rank
+ * ends with the full outputs the ncnn boundary hands on:
+ *   - window split: the windows sharing a (t-range, h-range) form a band --
+ *     frames x whole grid lines -- and bands in (t, h) order are cut into runs
+ *     of near-equal attention cost, one per rank, so a rank's video rows are a
+ *     few contiguous token runs; the fp32 text partial sums are all-reduced
+ *     (NCCL) and the video runs exchanged (below);
+ *   - head split, with fewer bands than ranks or fewer than 4 windows per rank:
+ *     each rank runs every window for a range of heads; the head slices of the
+ *     video and text outputs are exchanged.
+ * The video rows move either by NCCL all-gather (video_out in ordinary device
+ * memory) or, when video_out lies in a buffer from awa_comm_alloc_shared, as
+ * peer copies on the copy engines straight into every rank's copy, chunk by
+ * chunk behind the attention. No kernel reads a peer's memory; nothing uses
+ * TMA multicast. libnccl.so.2 is loaded on first use (inside a PyTorch
+ * process: the NCCL torch loaded). */
 typedef struct awa_comm awa_comm;
 
 /* ncclGetUniqueId: rank 0 calls it and hands the bytes (128) to every rank. */
@@ -277,8 +283,13 @@ int awa_comm_alloc_shared(awa_comm* comm, size_t bytes, void** ptr);
 int awa_comm_free_shared(awa_comm* comm, void* ptr);
 int awa_comm_info(const awa_comm* comm, int* rank, int* nranks);
 /* The split awa_forward_sharded uses for nranks ranks: *by_heads (0/1) and
- * nranks+1 bounds (window indices, or head indices for a head split). */
+ * nranks+1 bounds: head indices for a head split; for a window split the
+ * prefix sums of the ranks' window counts. */
 int awa_shard_split(const awa_plan* plan, int nranks, int heads, int* by_heads, int* bounds);
+/* The windows (ascending plan indices) that `rank` computes in a window split
+ * (every window for a head split): writes min(count, capacity), returns the
+ * count. */
+int awa_shard_windows(const awa_plan* plan, int nranks, int heads, int rank, int* windows, int capacity);
 size_t awa_forward_sharded_workspace_bytes(const awa_plan* plan, int nranks, int heads, int head_dim, int out_dtype);
 /* awa_forward over the ranks of `comm`: same arguments and outputs (on every
  * rank: inputs replicated, outputs complete), plus a workspace of

@@ -216,7 +216,8 @@ __global__ void __launch_bounds__(kThreads, 2) attention_simt_kernel(const AttnA
             else
             {
                 is_text = 1;
-                dst = ((int64_t)(item.x - a.window_begin) * text + (row - win.video)) * a.heads * hd + (int64_t)head * hd;
+                const int slot = a.partial_slot ? a.partial_slot[item.x] : item.x - a.window_begin;
+                dst = ((int64_t)slot * text + (row - win.video)) * a.heads * hd + (int64_t)head * hd;
             }
         }
         sh.q_dst[r] = dst;

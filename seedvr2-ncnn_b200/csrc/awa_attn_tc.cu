@@ -1039,8 +1039,8 @@ __device__ void softmax_role(const AttnArgs& a, TcShared& sh, int njobs, uint32_
                 else
                 {
                     text_row = true;
-                    dst = ((int64_t)(job.window - a.window_begin) * text + (geo.first + qi)) * a.heads * kHeadDim +
-                          (int64_t)job.head * kHeadDim;
+                    const int slot = a.partial_slot ? a.partial_slot[job.window] : job.window - a.window_begin;
+                    dst = ((int64_t)slot * text + (geo.first + qi)) * a.heads * kHeadDim + (int64_t)job.head * kHeadDim;
                 }
             }
         }

@@ -98,6 +98,9 @@ struct AttnArgs
     int* error_flag = nullptr;
     int out_v8 = 0;  // tcgen05 kernel: output rows (and text partials) are 32-byte aligned
     int rotate = 1;  // fused: 1 = rotate Q/K as they are loaded, 0 = they arrive rotated (awa_qkv_project_rotated)
+    // fused, a set of windows (multi-GPU): the text-partial slot of window w,
+    // instead of w - window_begin
+    const int* partial_slot = nullptr;
 };
 
 // Launchers (return a cudaError_t value as int).
@@ -159,6 +162,13 @@ int attention_range(const awa_plan* plan, int precision, int heads, int head_dim
                     const void* text_qkv, int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype,
                     void* video_out, int64_t video_token_stride_out, void* partials, size_t partial_bytes,
                     int* partial_dtype, cudaStream_t stream);
+// attention_range over a set of windows (sorted, distinct): the text
+// partials of the k-th window of the set go to slot k.
+int attention_set(const awa_plan* plan, int precision, int heads, int head_dim, const int* windows, int count,
+                  int in_dtype, const void* video_qkv, int64_t video_token_stride, int64_t video_qkv_stride,
+                  const void* text_qkv, int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype,
+                  void* video_out, int64_t video_token_stride_out, void* partials, size_t partial_bytes,
+                  int* partial_dtype, cudaStream_t stream);
 // fp32 sum over windows [window_begin, window_end) of dense partials (slot
 // w - window_begin), in window order, not divided.
 int text_partial_sum(const awa_plan* plan, int heads, int head_dim, int partial_dtype, const void* partials,

@@ -10,6 +10,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <deque>
 #include <limits>
 #include <mutex>
 #include <string>
@@ -45,8 +46,17 @@ struct awa_plan
     const int2* d_items_tc = nullptr;
     const int2* d_items_tc_packed = nullptr;
     const int2* d_items_simt = nullptr;
-    std::mutex range_mutex;  // guards the per-range item cache below
+    std::mutex range_mutex;  // guards the per-range and per-set caches below
     std::vector<std::pair<std::pair<int, int>, std::pair<int2*, int>>> range_items;  // (begin,end) -> items
+    struct SetEntry
+    {
+        bool tc;
+        std::vector<int> windows;  // sorted
+        int2* items;               // device, the set's work items
+        int count;
+        int* slots;                // device [W]: slot of each window in the set, -1 outside
+    };
+    std::deque<SetEntry> set_items;  // a deque: entries stay put while others are added
 };
 
 namespace
@@ -545,6 +555,11 @@ void awa_plan_destroy(awa_plan* plan)
     {
         for (auto& entry : plan->range_items)
             cudaFree(entry.second.first);
+        for (auto& entry : plan->set_items)
+        {
+            cudaFree(entry.items);
+            cudaFree(entry.slots);
+        }
         cudaFree(plan->device_block);
     }
     delete plan;
@@ -763,6 +778,49 @@ static const int2* range_items(awa_plan* plan, bool tc, int begin, int end, int*
     return d;
 }
 
+// Items and slot map of a window set (sorted, distinct), cached on the device.
+static const awa_plan::SetEntry* set_items(awa_plan* plan, bool tc, const int* windows, int n, int* rc)
+{
+    *rc = AWA_OK;
+    std::vector<int> key(windows, windows + n);
+    std::lock_guard<std::mutex> lock(plan->range_mutex);
+    for (const auto& e : plan->set_items)
+        if (e.tc == tc && e.windows == key)
+            return &e;
+    const int W = plan->info.window_count;
+    std::vector<int> slots(W, -1);
+    for (int k = 0; k < n; k++)
+    {
+        if (windows[k] < 0 || windows[k] >= W || (k > 0 && windows[k] <= windows[k - 1]))
+        {
+            *rc = fail(AWA_ERR_INVALID, "window set: indices must be sorted, distinct and < %d", W);
+            return nullptr;
+        }
+        slots[windows[k]] = k;
+    }
+    std::vector<int2> items;
+    for (const int2& item : tc ? plan->items_tc : plan->items_simt)
+        if (slots[item.x] >= 0)
+            items.push_back(item);
+    awa_plan::SetEntry e{tc, key, nullptr, (int)items.size(), nullptr};
+    cudaError_t err = cudaMalloc(&e.slots, bytes_of(slots));
+    if (err == cudaSuccess)
+        err = cudaMemcpy(e.slots, slots.data(), bytes_of(slots), cudaMemcpyHostToDevice);
+    if (err == cudaSuccess && !items.empty())
+        err = cudaMalloc(&e.items, bytes_of(items));
+    if (err == cudaSuccess && !items.empty())
+        err = cudaMemcpy(e.items, items.data(), bytes_of(items), cudaMemcpyHostToDevice);
+    if (err != cudaSuccess)
+    {
+        cudaFree(e.slots);
+        cudaFree(e.items);
+        *rc = cuda_fail(err, "window set work list");
+        return nullptr;
+    }
+    plan->set_items.push_back(std::move(e));
+    return &plan->set_items.back();
+}
+
 // Runs the fused attention over windows [window_begin, window_end); the text
 // rows' per-window outputs go to the workspace as partials of *partial_dtype
 // (bf16 from the tensor-core kernel, as the layer chain's bf16 attended rows;
@@ -771,7 +829,7 @@ static int forward_impl(const awa_plan* cplan, int precision, int heads, int hea
                         int window_end, int in_dtype, const void* video_qkv, int64_t vts, int64_t vqs,
                         const void* text_qkv, int64_t tts, int64_t tqs, int out_dtype, void* video_out,
                         int64_t vots, void* workspace, size_t workspace_bytes, int* partial_dtype,
-                        cudaStream_t stream, int rotate = 1)
+                        cudaStream_t stream, int rotate = 1, const int* window_set = nullptr, int set_count = 0)
 {
     awa_plan* plan = const_cast<awa_plan*>(cplan);
     const int64_t head_row = (int64_t)heads * head_dim;
@@ -782,7 +840,8 @@ static int forward_impl(const awa_plan* cplan, int precision, int heads, int hea
         return fail(AWA_ERR_INVALID, "awa_forward: strides smaller than a row");
     if (head_dim < plan->info.rope_dim)
         return fail(AWA_ERR_INVALID, "awa_forward: head_dim %d < rope_dim %d", head_dim, plan->info.rope_dim);
-    const size_t need = (size_t)(window_end - window_begin) * plan->info.text_tokens * head_row * sizeof(float);
+    const size_t need = (size_t)(window_set ? set_count : window_end - window_begin) * plan->info.text_tokens *
+                        head_row * sizeof(float);
     if (!workspace || workspace_bytes < need)
         return fail(AWA_ERR_INVALID, "awa_forward: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
     const bool tc = tc_capable(plan, precision, head_dim);
@@ -839,7 +898,18 @@ static int forward_impl(const awa_plan* cplan, int precision, int heads, int hea
     args.window_begin = window_begin;
     args.rotate = rotate;
     int count = 0, rc = AWA_OK;
-    const int2* items = range_items(plan, tc, window_begin, window_end, &count, &rc);
+    const int2* items = nullptr;
+    if (window_set)
+    {
+        const awa_plan::SetEntry* e = set_items(plan, tc, window_set, set_count, &rc);
+        if (rc)
+            return rc;
+        items = e->items;
+        count = e->count;
+        args.partial_slot = e->slots;
+    }
+    else
+        items = range_items(plan, tc, window_begin, window_end, &count, &rc);
     if (rc)
         return rc;
     return run_attention(plan, precision, args, 0, in_dtype, out_dtype, items, count, stream);
@@ -949,6 +1019,26 @@ int attention_range(const awa_plan* plan, int precision, int heads, int head_dim
     return forward_impl(plan, precision, heads, head_dim, window_begin, window_end, in_dtype, video_qkv,
                         video_token_stride, video_qkv_stride, text_qkv, text_token_stride, text_qkv_stride, out_dtype,
                         video_out, video_token_stride_out, partials, partial_bytes, partial_dtype, stream);
+}
+
+int attention_set(const awa_plan* plan, int precision, int heads, int head_dim, const int* windows, int count,
+                  int in_dtype, const void* video_qkv, int64_t video_token_stride, int64_t video_qkv_stride,
+                  const void* text_qkv, int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype,
+                  void* video_out, int64_t video_token_stride_out, void* partials, size_t partial_bytes,
+                  int* partial_dtype, cudaStream_t stream)
+{
+    int rc = check_heads(plan, heads, head_dim);
+    if (rc)
+        return rc;
+    if (count < 0 || (count > 0 && !windows) || !partial_dtype)
+        return fail(AWA_ERR_INVALID, "attention over a window set: invalid set");
+    *partial_dtype = awa_attention_kernel_kind(plan, precision, in_dtype, heads, head_dim) == 1 ? AWA_BF16 : AWA_F32;
+    if (count == 0)
+        return AWA_OK;
+    return forward_impl(plan, precision, heads, head_dim, 0, plan->info.window_count, in_dtype, video_qkv,
+                        video_token_stride, video_qkv_stride, text_qkv, text_token_stride, text_qkv_stride, out_dtype,
+                        video_out, video_token_stride_out, partials, partial_bytes, partial_dtype, stream, 1, windows,
+                        count);
 }
 
 int text_partial_sum(const awa_plan* plan, int heads, int head_dim, int partial_dtype, const void* partials,

@@ -29,9 +29,11 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <array>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <type_traits>
 #include <vector>
@@ -144,27 +146,118 @@ namespace
 {
 
 // How one layer is split over the ranks of a communicator.
+//
+// Window split: the windows tile the grid as a product of t-, h- and
+// w-intervals, so the windows sharing a (t-interval, h-interval) form a band:
+// frames [t0, t1) x grid lines [h0, h1) x every column. Bands in (t, h) order
+// are cut into nranks runs of near-equal attention cost (sum of L^2 over the
+// band's windows). A rank then owns whole grid lines: per frame of each of
+// its bands one contiguous run of tokens, merged across frames where a band
+// spans every line -- so its video rows leave it in a few large copies.
+struct Band
+{
+    int t0, t1, h0, h1;
+    double cost;               // sum of L^2 over its windows
+    std::vector<int> windows;  // plan indices, ascending
+};
+
 struct Split
 {
     bool by_heads = false;
-    std::vector<int> bounds;  // window bounds (nranks + 1) or head bounds (nranks + 1)
-    int64_t slot_rows = 0;    // window split: rows of one rank's slot of the gather buffer
+    std::vector<int> bounds;  // head split: head bounds; window split: windows before each rank (prefix sums)
+    std::vector<Band> bands;  // window split: in (t, h) order
+    std::vector<std::vector<int>> rank_bands;  // per rank: its bands, in order
+    std::vector<std::vector<int>> windows;     // per rank: its windows, ascending
+    int64_t slot_rows = 0;                     // most video rows of one rank
 };
+
+// The windows of some bands, ascending.
+std::vector<int> band_windows(const Split& s, const int* bands, int n)
+{
+    std::vector<int> w;
+    for (int i = 0; i < n; i++)
+        w.insert(w.end(), s.bands[bands[i]].windows.begin(), s.bands[bands[i]].windows.end());
+    std::sort(w.begin(), w.end());
+    return w;
+}
+
+// The token runs (first token, tokens) of some bands, in order, adjacent runs merged.
+std::vector<std::pair<int64_t, int64_t>> band_runs(const Split& s, const awa_plan_info& info, const int* bands, int n)
+{
+    std::vector<std::pair<int64_t, int64_t>> runs;
+    const int64_t line = info.source_w;
+    for (int i = 0; i < n; i++)
+    {
+        const Band& b = s.bands[bands[i]];
+        for (int t = b.t0; t < b.t1; t++)
+        {
+            const int64_t first = ((int64_t)t * info.source_h + b.h0) * line, count = (int64_t)(b.h1 - b.h0) * line;
+            if (!runs.empty() && runs.back().first + runs.back().second == first)
+                runs.back().second += count;
+            else
+                runs.emplace_back(first, count);
+        }
+    }
+    return runs;
+}
 
 Split make_split(const awa_plan* plan, const awa_plan_info& info, int nranks, int heads)
 {
     Split s;
     s.bounds.assign(nranks + 1, 0);
-    s.by_heads = nranks > 1 && info.window_count < 4 * nranks && heads >= nranks;
+    std::vector<awa_window> win(info.window_count);
+    awa_plan_get_maps(plan, nullptr, nullptr, nullptr, nullptr, win.data());
+    {
+        std::map<std::array<int, 4>, size_t> index;
+        for (int w = 0; w < info.window_count; w++)
+        {
+            const awa_window& x = win[w];
+            const std::array<int, 4> key{x.t0, x.h0, x.t1, x.h1};
+            auto it = index.find(key);
+            if (it == index.end())
+            {
+                it = index.emplace(key, s.bands.size()).first;
+                s.bands.push_back(Band{x.t0, x.t1, x.h0, x.h1, 0.0, {}});
+            }
+            Band& b = s.bands[it->second];
+            const double L = (double)(x.t1 - x.t0) * (x.h1 - x.h0) * (x.w1 - x.w0) + info.text_tokens;
+            b.cost += L * L;
+            b.windows.push_back(w);
+        }
+        std::sort(s.bands.begin(), s.bands.end(),
+                  [](const Band& a, const Band& b) { return a.t0 != b.t0 ? a.t0 < b.t0 : a.h0 < b.h0; });
+    }
+    s.by_heads = nranks > 1 && heads >= nranks && ((int)s.bands.size() < nranks || info.window_count < 4 * nranks);
     if (s.by_heads)
     {
         for (int r = 0; r <= nranks; r++)
             s.bounds[r] = (int)((int64_t)heads * r / nranks);
         return s;
     }
-    awa_partition_windows(plan, nranks, s.bounds.data());
+    // bands -> ranks in order: each band goes to the rank whose equal share of
+    // the total cost its cost midpoint falls in
+    double total = 0;
+    for (const Band& b : s.bands)
+        total += b.cost;
+    s.rank_bands.assign(nranks, {});
+    double acc = 0;
+    for (size_t i = 0; i < s.bands.size(); i++)
+    {
+        const double mid = acc + 0.5 * s.bands[i].cost;
+        s.rank_bands[std::min(nranks - 1, (int)(mid / total * nranks))].push_back((int)i);
+        acc += s.bands[i].cost;
+    }
+    s.windows.resize(nranks);
     for (int r = 0; r < nranks; r++)
-        s.slot_rows = std::max<int64_t>(s.slot_rows, awa_window_range_video_rows(plan, s.bounds[r], s.bounds[r + 1]));
+    {
+        const auto& rb = s.rank_bands[r];
+        s.windows[r] = band_windows(s, rb.data(), (int)rb.size());
+        int64_t rows = 0;
+        for (const auto& run : band_runs(s, info, rb.data(), (int)rb.size()))
+            rows += run.second;
+        s.slot_rows = std::max(s.slot_rows, rows);
+        s.bounds[r + 1] = s.bounds[r] + (int)s.windows[r].size();
+    }
     return s;
 }
 
@@ -197,10 +290,10 @@ Layout make_layout(const awa_plan* plan, const awa_plan_info& info, const Split&
     }
     else
     {
-        int most = 0;
-        for (int r = 0; r < nranks; r++)
-            most = std::max(most, s.bounds[r + 1] - s.bounds[r]);
-        off += align256((size_t)std::max(most, 1) * info.text_tokens * row * sizeof(float));
+        size_t most = 1;
+        for (const auto& w : s.windows)
+            most = std::max(most, w.size());
+        off += align256(most * info.text_tokens * row * sizeof(float));
         l.gather = off;
         off += align256((size_t)nranks * std::max<int64_t>(s.slot_rows, 1) * row * dsize(out_dtype));
         l.text_gather = off;
@@ -254,93 +347,45 @@ int push_streams(awa_comm* c)
     return cuda_status(e, "peer copy stream");
 }
 
-// Chunk boundaries of windows [w0, w1): up to kPushChunks runs of near-equal
-// attention cost (sum of L^2, L = video rows; the text rows add the same to
-// every window of one shape).
-std::vector<int> push_chunks(const std::vector<awa_window>& win, int w0, int w1)
+// The rank's bands cut into at most kPushChunks runs of near-equal cost:
+// returns the band-list offsets of the cuts (first 0, last the band count).
+std::vector<int> push_chunks(const Split& s, int rank)
 {
-    std::vector<double> cost;
+    const auto& rb = s.rank_bands[rank];
     double total = 0;
-    for (int w = w0; w < w1; w++)
-    {
-        const double L = (double)(win[w].t1 - win[w].t0) * (win[w].h1 - win[w].h0) * (win[w].w1 - win[w].w0);
-        cost.push_back(L * L);
-        total += L * L;
-    }
-    const int chunks = std::max(1, std::min(kPushChunks, (w1 - w0) / 8));
-    std::vector<int> cuts{w0};
+    for (int b : rb)
+        total += s.bands[b].cost;
+    const int chunks = std::max(1, std::min<int>(kPushChunks, (int)rb.size()));
+    std::vector<int> cuts{0};
     double acc = 0;
-    int w = w0;
-    for (int c = 1; c < chunks; c++)
+    for (size_t i = 0; i < rb.size(); i++)
     {
-        while (w < w1 && acc + 0.5 * cost[w - w0] < total * c / chunks)
-            acc += cost[w++ - w0];
-        if (w > cuts.back())
-            cuts.push_back(w);
+        acc += s.bands[rb[i]].cost;
+        const int c = (int)cuts.size();
+        if (c < chunks && i + 1 < rb.size() && acc >= total * c / chunks)
+            cuts.push_back((int)i + 1);
     }
-    if (w1 > cuts.back())
-        cuts.push_back(w1);
+    cuts.push_back((int)rb.size());
     return cuts;
 }
 
-// Copies the video rows of windows [wb, we) from `local` into every peer, on
-// the side stream once the attention that wrote them (enqueued on `st`) is
-// done. Windows in plan order run t fastest, then h, then w: runs of windows
-// are merged into boxes (t0..t1, h0..h1, w0..w1) first along t, then h, then w,
-// and each box goes as one pitched copy per frame per peer.
-int push_rows(awa_comm* c, const std::vector<awa_window>& win, int wb, int we, unsigned char* local,
-              const std::vector<unsigned char*>& peers, int64_t line_bytes, int64_t frame_bytes, int64_t token_bytes,
-              int64_t row_bytes, size_t chunk, cudaStream_t st)
+// Copies token runs of video rows from `local` into every peer at the same
+// offsets, on the side stream once the work enqueued so far on `st` is done.
+// A run is one contiguous byte range (its tokens' rows and the padding between
+// them), so each goes as a single peer copy.
+int push_runs(awa_comm* c, const std::vector<std::pair<int64_t, int64_t>>& runs, unsigned char* local,
+              const std::vector<unsigned char*>& peers, int64_t token_bytes, int64_t row_bytes, size_t chunk,
+              cudaStream_t st)
 {
-    std::vector<awa_window> boxes;
-    for (int w = wb; w < we; w++)
-    {
-        const awa_window& x = win[w];
-        if (!boxes.empty())
-        {
-            awa_window& b = boxes.back();
-            if (b.h0 == x.h0 && b.h1 == x.h1 && b.w0 == x.w0 && b.w1 == x.w1 && b.t1 == x.t0)
-            {
-                b.t1 = x.t1;
-                continue;
-            }
-            if (b.t0 == x.t0 && b.t1 == x.t1 && b.w0 == x.w0 && b.w1 == x.w1 && b.h1 == x.h0)
-            {
-                b.h1 = x.h1;
-                continue;
-            }
-        }
-        boxes.push_back(x);
-    }
-    // boxes that follow each other along w
-    std::vector<awa_window> merged;
-    for (const awa_window& x : boxes)
-    {
-        if (!merged.empty())
-        {
-            awa_window& b = merged.back();
-            if (b.t0 == x.t0 && b.t1 == x.t1 && b.h0 == x.h0 && b.h1 == x.h1 && b.w1 == x.w0)
-            {
-                b.w1 = x.w1;
-                continue;
-            }
-        }
-        merged.push_back(x);
-    }
     cudaError_t e = cudaEventRecord(c->push_events[chunk], st);
     if (e == cudaSuccess)
         e = cudaStreamWaitEvent(c->push_stream, c->push_events[chunk], 0);
-    for (const awa_window& b : merged)
+    for (const auto& run : runs)
     {
-        const int64_t width = (int64_t)(b.w1 - b.w0 - 1) * token_bytes + row_bytes;
-        for (int t = b.t0; t < b.t1 && e == cudaSuccess; t++)
-        {
-            const int64_t off = t * frame_bytes + b.h0 * line_bytes + b.w0 * token_bytes;
-            for (unsigned char* peer : peers)
-                if (e == cudaSuccess)
-                    e = cudaMemcpy2DAsync(peer + off, line_bytes, local + off, line_bytes, width, b.h1 - b.h0,
-                                          cudaMemcpyDeviceToDevice, c->push_stream);
-        }
+        const int64_t off = run.first * token_bytes, bytes = (run.second - 1) * token_bytes + row_bytes;
+        for (unsigned char* peer : peers)
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(peer + off, local + off, (size_t)bytes, cudaMemcpyDeviceToDevice, c->push_stream);
     }
     return cuda_status(e, "peer copy of video rows");
 }
@@ -566,6 +611,24 @@ int awa_shard_split(const awa_plan* plan, int nranks, int heads, int* by_heads, 
     return AWA_OK;
 }
 
+int awa_shard_windows(const awa_plan* plan, int nranks, int heads, int rank, int* windows, int capacity)
+{
+    awa_plan_info info;
+    if (!plan || nranks <= 0 || heads <= 0 || rank < 0 || rank >= nranks || capacity < 0 ||
+        (capacity > 0 && !windows) || awa_plan_get_info(plan, &info) != AWA_OK)
+        return fail(AWA_ERR_INVALID, "awa_shard_windows: invalid arguments");
+    const Split s = make_split(plan, info, nranks, heads);
+    if (s.by_heads)
+    {
+        for (int w = 0; w < std::min(capacity, info.window_count); w++)
+            windows[w] = w;
+        return info.window_count;
+    }
+    const auto& mine = s.windows[rank];
+    std::copy(mine.begin(), mine.begin() + std::min<size_t>(capacity, mine.size()), windows);
+    return (int)mine.size();
+}
+
 size_t awa_forward_sharded_workspace_bytes(const awa_plan* plan, int nranks, int heads, int head_dim, int out_dtype)
 {
     awa_plan_info info;
@@ -627,7 +690,6 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
         if ((rc = push_streams(comm)) != AWA_OK || (rc = barrier(n, comm, st)) != AWA_OK)
             return rc;
     }
-    const int64_t line_bytes = (int64_t)info.source_w * video_token_stride_out * osz;  // one grid line of tokens
 
     if (s.by_heads)
     {
@@ -702,8 +764,9 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
         return rc;
     }
 
-    // Window split: this rank's windows [w0, w1).
-    const int w0 = s.bounds[r], w1 = s.bounds[r + 1];
+    // Window split: this rank's bands (whole grid lines of every frame they span).
+    const std::vector<int>& mine = s.windows[r];
+    const int64_t tbytes = video_token_stride_out * (int64_t)osz, rbytes = row * (int64_t)osz;
     float* text_sum = reinterpret_cast<float*>(ws + l.text_sum);
     unsigned char* partials = ws + l.forward;
     const size_t partial_bytes = l.gather - l.forward;
@@ -711,26 +774,29 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
     int partial_dtype = AWA_F32;
     if (direct)
     {
-        std::vector<awa_window> windows(info.window_count);
-        awa_plan_get_maps(plan, nullptr, nullptr, nullptr, nullptr, windows.data());
-        const std::vector<int> cuts = push_chunks(windows, w0, w1);
+        // chunk by chunk: attention of the chunk's windows, then its rows to the
+        // peers on the side stream while the next chunk computes
+        const std::vector<int> cuts = push_chunks(s, r);
+        const auto& rb = s.rank_bands[r];
+        const size_t psz = awa_attention_kernel_kind(plan, precision, in_dtype, heads, head_dim) == 1 ? 2 : 4;
+        size_t done = 0;  // windows (partial slots) of the chunks so far
         for (size_t c = 0; c + 1 < cuts.size() && rc == AWA_OK; c++)
         {
-            const int cb = cuts[c], ce = cuts[c + 1];
-            int pd = AWA_F32;
-            const size_t psz_guess = awa_attention_kernel_kind(plan, precision, in_dtype, heads, head_dim) == 1 ? 2 : 4;
-            const size_t off = (size_t)(cb - w0) * window_partial * psz_guess;
-            rc = awa::attention_range(plan, precision, heads, head_dim, cb, ce, in_dtype, video_qkv,
-                                      video_token_stride, video_qkv_stride, text_qkv, text_token_stride,
-                                      text_qkv_stride, out_dtype, video_out, video_token_stride_out, partials + off,
-                                      partial_bytes - off, &pd, st);
-            partial_dtype = pd;
+            const std::vector<int> set = band_windows(s, rb.data() + cuts[c], cuts[c + 1] - cuts[c]);
+            const size_t off = done * window_partial * psz;
+            rc = awa::attention_set(plan, precision, heads, head_dim, set.data(), (int)set.size(), in_dtype,
+                                    video_qkv, video_token_stride, video_qkv_stride, text_qkv, text_token_stride,
+                                    text_qkv_stride, out_dtype, video_out, video_token_stride_out, partials + off,
+                                    partial_bytes - off, &partial_dtype, st);
+            done += set.size();
             if (rc == AWA_OK)
-                rc = push_rows(comm, windows, cb, ce, static_cast<unsigned char*>(video_out), peers, line_bytes,
-                               (int64_t)info.source_h * line_bytes, video_token_stride_out * osz, row * osz, c, st);
+                rc = push_runs(comm, band_runs(s, info, rb.data() + cuts[c], cuts[c + 1] - cuts[c]),
+                               static_cast<unsigned char*>(video_out), peers, tbytes, rbytes, c, st);
         }
+        // the chunks' partial slots run in band order; the sum over all of them
+        // covers this rank's windows once each
         if (rc == AWA_OK)
-            rc = awa::text_partial_sum(plan, heads, head_dim, partial_dtype, partials, w0, w1, text_sum, st);
+            rc = awa::text_partial_sum(plan, heads, head_dim, partial_dtype, partials, 0, (int)done, text_sum, st);
         if (rc == AWA_OK)
             rc = join_pushes(comm, st);
         if (rc == AWA_OK)
@@ -742,15 +808,37 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
         return awa_text_finalize(plan, heads, head_dim, text_sum, out_dtype, text_out, text_token_stride_out, stream);
     }
 
-    rc = awa_forward_windows(plan, precision, heads, head_dim, w0, w1, in_dtype, video_qkv, video_token_stride,
-                             video_qkv_stride, text_qkv, text_token_stride, text_qkv_stride, out_dtype, video_out,
-                             video_token_stride_out, text_sum, partials, partial_bytes, stream);
+    // All-gather mode: attention of this rank's windows, its runs packed into its
+    // slot of the gather buffer, NCCL all-gather of the slots and all-reduce of
+    // the text partial sums, the other ranks' runs copied back into place.
+    rc = awa::attention_set(plan, precision, heads, head_dim, mine.data(), (int)mine.size(), in_dtype, video_qkv,
+                            video_token_stride, video_qkv_stride, text_qkv, text_token_stride, text_qkv_stride,
+                            out_dtype, video_out, video_token_stride_out, partials, partial_bytes, &partial_dtype, st);
+    if (rc == AWA_OK)
+        rc = awa::text_partial_sum(plan, heads, head_dim, partial_dtype, partials, 0, (int)mine.size(), text_sum, st);
     if (rc)
         return rc;
     unsigned char* gather = ws + l.gather;
-    const size_t slot = (size_t)s.slot_rows * row;  // elements
-    rc = awa_gather_video_shard(plan, heads, head_dim, w0, w1, out_dtype, video_out, video_token_stride_out,
-                                gather + r * slot * osz, stream);
+    const size_t slot_bytes = (size_t)std::max<int64_t>(s.slot_rows, 1) * rbytes;  // dense rows
+    auto copy_runs = [&](int q, bool to_slot) {
+        const auto runs = band_runs(s, info, s.rank_bands[q].data(), (int)s.rank_bands[q].size());
+        unsigned char* slot = gather + q * slot_bytes;
+        int64_t at = 0;
+        int result = AWA_OK;
+        for (const auto& run : runs)
+        {
+            unsigned char* v = static_cast<unsigned char*>(video_out) + run.first * tbytes;
+            if (result == AWA_OK)
+                result = cuda_status(to_slot ? cudaMemcpy2DAsync(slot + at, rbytes, v, tbytes, rbytes, run.second,
+                                                                 cudaMemcpyDeviceToDevice, st)
+                                             : cudaMemcpy2DAsync(v, tbytes, slot + at, rbytes, rbytes, run.second,
+                                                                 cudaMemcpyDeviceToDevice, st),
+                                     "video run copy");
+            at += run.second * rbytes;
+        }
+        return result;
+    };
+    rc = copy_runs(r, true);
     if (rc)
         return rc;
     rc = nccl_status(n, n->group_start(), "ncclGroupStart");
@@ -758,8 +846,8 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
         rc = nccl_status(n, n->all_reduce(text_sum, text_sum, (size_t)info.text_tokens * row, ncclFloat32, ncclSum,
                                           comm->comm, st),
                          "ncclAllReduce (text partial sums)");
-    if (rc == AWA_OK && slot > 0)
-        rc = nccl_status(n, n->all_gather(gather + r * slot * osz, gather, slot, otype, comm->comm, st),
+    if (rc == AWA_OK)
+        rc = nccl_status(n, n->all_gather(gather + r * slot_bytes, gather, slot_bytes, ncclUint8, comm->comm, st),
                          "ncclAllGather (video rows)");
     const int end_rc = nccl_status(n, n->group_end(), "ncclGroupEnd");
     rc = rc ? rc : end_rc;
@@ -768,8 +856,7 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
     rc = awa_text_finalize(plan, heads, head_dim, text_sum, out_dtype, text_out, text_token_stride_out, stream);
     for (int q = 0; q < R && rc == AWA_OK; q++)
         if (q != r)
-            rc = awa_scatter_video_shard(plan, heads, head_dim, s.bounds[q], s.bounds[q + 1], out_dtype,
-                                         gather + q * slot * osz, video_out, video_token_stride_out, stream);
+            rc = copy_runs(q, false);
     return rc;
 }
 

@@ -1,9 +1,9 @@
 """Two-rank (gloo, CPU) test of the multi-GPU protocol of awa_forward_sharded.
 
-On GPUs the split comes from awa_shard_split. With enough windows, rank r
-computes windows [bounds[r], bounds[r+1)) (awa_forward_windows: its video rows
-+ an unnormalised fp32 text partial sum), the ranks all-reduce the partial,
-divide by the window count and all-gather the video rows. With fewer than 4
+On GPUs the split comes from awa_shard_split / awa_shard_windows. With enough
+windows, rank r computes the windows of its bands (runs of whole grid lines:
+its video rows + an unnormalised fp32 text partial sum), the ranks all-reduce
+the partial, divide by the window count and exchange the video rows. With fewer than 4
 windows per rank, rank r computes every window for heads [bounds[r],
 bounds[r+1)) and the ranks all-gather the head slices. Here each rank runs the
 same protocol on the CPU with the oracle standing in for the kernels: the
@@ -94,10 +94,12 @@ def _rank_main(rank: int, world: int, port: int, case, result_dir: str):
             attended[:, begin:end] = att
             windows = range(W)
         else:
+            # this rank's bands: the windows awa_shard_windows names
+            windows = plan.shard_windows(world, h, rank)
+            assert len(windows) == end - begin and windows == sorted(windows)
             attended = np.zeros((len(seq), h, d), np.float32)
-            if end > begin:
-                oracle.attention_range(roped, cu, begin, end, h, d, attended)
-            windows = range(begin, end)
+            for w in windows:
+                oracle.attention_range(roped, cu, w, w + 1, h, d, attended)
         heads_owned = slice(begin, end) if by_heads else slice(0, h)
         partial = np.zeros((text, h, d), np.float32)
         for w in windows:
@@ -106,7 +108,7 @@ def _rank_main(rank: int, world: int, port: int, case, result_dir: str):
             owned[seq[rows], heads_owned] += 1
             partial += attended[cu[w + 1] - text:cu[w + 1]]  # window order, fp32
         if not by_heads:
-            assert int(owned[:, 0].sum()) == plan.range_video_rows(begin, end)
+            assert int(owned[:, 0].sum()) == sum(plan.range_video_rows(w, w + 1) for w in windows)
         # the exchange: all-reduce of the partials (a head split's are disjoint),
         # all-gather of the video rows
         total = torch.from_numpy(partial)
