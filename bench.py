@@ -8,18 +8,21 @@ MMRoPE -> WindowAttention -> Unpack, run as the fused chain awa_forward --
 over one synthetic batch of the workload's shape, inputs resident in HBM.
 
 * value      windows of all ranks / max-over-ranks device time (CUDA events)
-* e2e        same metric through the C ABI with host buffers: pinned-host ->
-             device copy of the step's QKV, the forward, device -> host copy of
-             the outputs, every step inside the timed region; steps pipelined
-             over two device buffer sets (copy in of the next step and copy out
-             of the previous one overlap the forward and each other)
+* e2e        same metric through the C ABI with host buffers (awa_forward_host:
+             copy of the step's QKV from pinned host memory, the forward, copy
+             of the outputs back, every step inside the timed region); steps
+             alternate over two streams and device workspaces (copy in of the
+             next step and copy out of the previous one overlap the forward)
 * roofline   the dominant kernel (fused tcgen05 attention), timed live by the
              library's launch profiler (events on its own stream)
 * cpu_baseline  the reference's own awa_layers.cpp CPU forward (oracle/_ref),
              on a bounded sample of cfg4-shaped windows, scaled by sum(L^2)
 
-N > 1 (torchrun, one rank per GPU): every rank runs its own layer instance (an
-independent clip / CFG branch): weak scaling, no collective on the data path.
+N > 1 (torchrun, one rank per GPU): one layer split over the N GPUs
+(awa_forward_sharded: bands of windows per rank, NCCL all-reduce of the text
+partial sums, the video rows pushed to every rank by peer copies, or NCCL
+all-gather with --exchange nccl) -- strong scaling; --mode replicas runs an
+independent layer per GPU instead (weak scaling).
 --impl reference times the reference CPU path on all host cores (rank 0 only).
 """
 
@@ -513,7 +516,13 @@ def run_b200(args, rank, world, local_rank):
     launches = sum(v[0] for v in prof.values())
 
     # ---- end to end through the C ABI with host buffers (skipped by --no-e2e,
-    # for profiler captures that should hold little device memory)
+    # for profiler captures that should hold little device memory):
+    # awa_forward_host takes the pinned host QKV and output buffers and
+    # enqueues copy in, forward and copy out on its stream. Steps alternate
+    # over two streams and two device workspaces, as a stream of layers would
+    # run: the copy in of step i + 1 overlaps the forward of step i and the copy
+    # out of step i - 1 (the host link is full duplex). Every step copies its
+    # whole input in and its whole output out inside the timed region.
     e2e_ms, e2e_steps = None, 0
     if not args.no_e2e:
         e2e_steps = max(3, min(args.steps, args.e2e_steps))
@@ -521,43 +530,15 @@ def run_b200(args, rank, world, local_rank):
         host_t = torch.empty(text_qkv.shape, dtype=text_qkv.dtype, pin_memory=True)
         host_v.copy_(video_qkv)
         host_t.copy_(text_qkv)
-        out_v = torch.empty(video_out.shape, dtype=dtype, pin_memory=True)
-        out_t = torch.empty(text_out.shape, dtype=dtype, pin_memory=True)
-        # Steps are pipelined as a stream of layers would be: two device buffer
-        # sets; the host->device copy of step i + 1 (copy stream) runs while step i
-        # computes and while the device->host copy of step i - 1 (a second copy
-        # stream; PCIe is full duplex) drains. Every step still copies its whole
-        # input in and its whole output out inside the timed region.
-        dev_in = [(torch.empty_like(video_qkv), torch.empty_like(text_qkv)) for _ in range(2)]
-        dev_out = [(torch.empty_like(video_out), torch.empty_like(text_out)) for _ in range(2)]
-        h2d_stream, d2h_stream = torch.cuda.Stream(device), torch.cuda.Stream(device)
-        in_free, out_free = [None, None], [None, None]  # events: last reader of buffer set b done
+        outs = [(torch.empty(video_out.shape, dtype=dtype, pin_memory=True),
+                 torch.empty(text_out.shape, dtype=dtype, pin_memory=True)) for _ in range(2)]
+        streams = [torch.cuda.Stream(device), torch.cuda.Stream(device)]
+        need = plan.host_workspace_bytes(prec, in_dtype, dtype, HEADS, HEAD_DIM)
+        spaces = [torch.empty(need, dtype=torch.uint8, device=device) for _ in range(2)]
 
         def e2e_step(i):
             b = i % 2
-            dv, dt = dev_in[b]
-            ov, ot = dev_out[b]
-            with torch.cuda.stream(h2d_stream):
-                if in_free[b] is not None:
-                    h2d_stream.wait_event(in_free[b])
-                dv.copy_(host_v, non_blocking=True)
-                dt.copy_(host_t, non_blocking=True)
-                loaded = torch.cuda.Event()
-                loaded.record(h2d_stream)
-            stream.wait_event(loaded)
-            if out_free[b] is not None:
-                stream.wait_event(out_free[b])
-            plan.forward(dv, dt, prec, out_dtype=dtype, workspace=workspace, video_out=ov, text_out=ot, stream=stream)
-            computed = torch.cuda.Event()
-            computed.record(stream)
-            in_free[b] = computed
-            with torch.cuda.stream(d2h_stream):
-                d2h_stream.wait_event(computed)
-                out_v.copy_(ov, non_blocking=True)
-                out_t.copy_(ot, non_blocking=True)
-                drained = torch.cuda.Event()
-                drained.record(d2h_stream)
-                out_free[b] = drained
+            plan.forward_host(host_v, host_t, outs[b][0], outs[b][1], prec, workspace=spaces[b], stream=streams[b])
 
         for i in range(2):
             e2e_step(i)
@@ -565,11 +546,14 @@ def run_b200(args, rank, world, local_rank):
         barrier()
         e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e_start.record(stream)
-        h2d_stream.wait_event(e_start)
-        d2h_stream.wait_event(e_start)
+        for st in streams:
+            st.wait_event(e_start)
         for i in range(e2e_steps):
             e2e_step(i)
-        stream.wait_event(out_free[(e2e_steps - 1) % 2])
+        for st in streams:
+            done = torch.cuda.Event()
+            done.record(st)
+            stream.wait_event(done)
         e_stop.record(stream)
         torch.cuda.synchronize()
         barrier()

@@ -169,6 +169,23 @@ int awa_forward_prerotated(const awa_plan* plan, int precision, int heads, int h
                            int64_t text_token_stride_out, void* workspace, size_t workspace_bytes,
                            awa_stream_t stream);
 
+/* awa_forward on HOST buffers -- the counterpart of the reference layers'
+ * CPU forward, whose blobs are host Mats (awa_layers.cpp:419-458, 638-689,
+ * 913-953, 1062-1120): video_qkv, text_qkv, video_out and text_out are host
+ * pointers (pinned memory lets the copies run at the host link's rate and
+ * overlap other streams); the call enqueues on `stream` the copies of the
+ * QKV rows in, the fused forward and the copies of the outputs back, and
+ * returns without waiting. device_workspace: awa_forward_host_workspace_bytes()
+ * bytes of device memory (the device copies and awa_forward's workspace); the
+ * host buffers must stay valid until the stream has done the work. */
+size_t awa_forward_host_workspace_bytes(const awa_plan* plan, int precision, int in_dtype, int out_dtype, int heads,
+                                        int head_dim);
+int awa_forward_host(const awa_plan* plan, int precision, int heads, int head_dim, int in_dtype,
+                     const void* video_qkv, int64_t video_token_stride, int64_t video_qkv_stride, const void* text_qkv,
+                     int64_t text_token_stride, int64_t text_qkv_stride, int out_dtype, void* video_out,
+                     int64_t video_token_stride_out, void* text_out, int64_t text_token_stride_out,
+                     void* device_workspace, size_t workspace_bytes, awa_stream_t stream);
+
 /* Size of the scratch that awa_forward_noalloc uses: 32 MiB of device memory
  * per GPU that loads this library, held until the process exits. */
 #define AWA_NOALLOC_SCRATCH_BYTES (32u << 20)

@@ -40,7 +40,8 @@ EXPORTED_SYMBOLS = (
     "awa_make_windows", "awa_plan_create", "awa_plan_create_host", "awa_plan_destroy", "awa_plan_get_info", "awa_plan_get_maps",
     "awa_pack", "awa_mmrope", "awa_window_attention", "awa_unpack", "awa_forward_workspace_bytes", "awa_forward",
     "awa_forward_workspace_bytes_for",
-    "awa_forward_noalloc", "awa_forward_prerotated", "awa_qkv_project_rotated",
+    "awa_forward_noalloc", "awa_forward_prerotated", "awa_qkv_project_rotated", "awa_forward_host",
+    "awa_forward_host_workspace_bytes",
     "awa_forward_windows", "awa_text_finalize", "awa_scatter_video_shard", "awa_gather_video_shard",
     "awa_window_range_video_rows", "awa_partition_windows", "awa_qkv_project", "awa_out_project", "awa_device_status",
     "awa_selftest_bounded_wait", "awa_attention_kernel_kind",
@@ -129,6 +130,8 @@ def library() -> ctypes.CDLL:
         "awa_forward": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p, sz, p]),
         "awa_forward_noalloc": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p]),
         "awa_forward_prerotated": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p, sz, p]),
+        "awa_forward_host": (i, [p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p, sz, p]),
+        "awa_forward_host_workspace_bytes": (sz, [p, i, i, i, i, i]),
         "awa_qkv_project_rotated": (i, [i, i, i, i, p, i64, p, i64, p, p, ctypes.c_float, p, i, i, p, i64, p]),
         "awa_qkv_project": (i, [i, i, i, i, p, i64, p, i64, p, p, ctypes.c_float, i, p, i64, p]),
         "awa_out_project": (i, [i, i, i, p, i64, p, i64, p, p, p, i64, i, i, p, i64, p]),
@@ -374,6 +377,30 @@ class AwaPlan:
                                      workspace.data_ptr(), workspace.numel() * workspace.element_size(),
                                      _stream_ptr(stream)))
         return video_out, text_out
+
+    def host_workspace_bytes(self, precision, in_dtype, out_dtype, heads: int, head_dim: int) -> int:
+        return int(library().awa_forward_host_workspace_bytes(self._handle, precision, _dtype_code_of(in_dtype),
+                                                              _dtype_code_of(out_dtype), heads, head_dim))
+
+    def forward_host(self, video_qkv, text_qkv, video_out, text_out, precision=AWA_PREC_BF16, workspace=None,
+                     stream=None):
+        """awa_forward_host: inputs and outputs are CPU tensors (pin them for
+        full-rate copies); enqueues copy in, forward and copy out on `stream`
+        without waiting. Returns the device workspace used (keep it alive until
+        the stream is done)."""
+        torch = _torch()
+        heads, hd = video_qkv.shape[2], video_qkv.shape[3]
+        if workspace is None:
+            need = self.host_workspace_bytes(precision, video_qkv.dtype, video_out.dtype, heads, hd)
+            workspace = torch.empty(max(need, 16), dtype=torch.uint8, device="cuda")
+        vts, vqs = _qkv_strides(video_qkv)
+        tts, tqs = _qkv_strides(text_qkv)
+        _check(library().awa_forward_host(self._handle, precision, heads, hd, _dtype_code(video_qkv),
+                                          video_qkv.data_ptr(), vts, vqs, text_qkv.data_ptr(), tts, tqs,
+                                          _dtype_code(video_out), video_out.data_ptr(), video_out.stride(0),
+                                          text_out.data_ptr(), text_out.stride(0), workspace.data_ptr(),
+                                          workspace.numel() * workspace.element_size(), _stream_ptr(stream)))
+        return workspace
 
     def forward_prerotated(self, video_qkv, text_qkv, precision=AWA_PREC_BF16, out_dtype=None, workspace=None,
                            video_out=None, text_out=None, stream=None):

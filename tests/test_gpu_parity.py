@@ -200,3 +200,30 @@ def test_fp32_qkv_in_a_bf16_block_takes_the_tensor_cores(cfg, results):
     with pytest.raises(awa_b200.AwaError, match="awa_forward_workspace_bytes_for"):
         plan.forward(dv, dt, AWA_PREC_BF16, workspace=small)
     awa_b200.device_status()
+
+
+@pytest.mark.parametrize("cfg", [CASES[4], CASES[1]], ids=case_id)
+def test_forward_on_host_buffers(cfg, results):
+    """awa_forward_host (host blobs, as the reference layers' CPU forward takes
+    them): the same outputs as awa_forward on device copies, bit for bit, with
+    dense host rows and with the qkv-major encoding's strides."""
+    bf16 = cfg.head_dim == 128
+    v, t, _ = results(cfg, bf16)
+    plan = plan_for(cfg)
+    prec, dtype = (AWA_PREC_BF16, torch.bfloat16) if bf16 else (AWA_PREC_FP32, torch.float32)
+    ref_v, ref_t = plan.forward(to_device(v, dtype), to_device(t, dtype), prec, out_dtype=torch.float32)
+    for layout in ("dense", "qkv-major"):
+        hv = torch.from_numpy(np.ascontiguousarray(v)).to(dtype)
+        ht = torch.from_numpy(np.ascontiguousarray(t)).to(dtype)
+        if layout == "qkv-major":
+            hv = hv.permute(1, 0, 2, 3).contiguous().permute(1, 0, 2, 3)
+            ht = ht.permute(1, 0, 2, 3).contiguous().permute(1, 0, 2, 3)
+        hv, ht = hv.pin_memory(), ht.pin_memory()
+        out_v = torch.empty(cfg.source_tokens, cfg.heads, cfg.head_dim).pin_memory()
+        out_t = torch.empty(cfg.text_tokens, cfg.heads, cfg.head_dim).pin_memory()
+        stream = torch.cuda.Stream()
+        plan.forward_host(hv, ht, out_v, out_t, prec, stream=stream)
+        stream.synchronize()
+        awa_b200.device_status()
+        assert torch.equal(out_v, ref_v.cpu()), layout
+        assert torch.equal(out_t, ref_t.cpu()), layout
