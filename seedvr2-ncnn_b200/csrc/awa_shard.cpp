@@ -181,23 +181,26 @@ std::vector<int> band_windows(const Split& s, const int* bands, int n)
     return w;
 }
 
-// The token runs (first token, tokens) of some bands, in order, adjacent runs merged.
+// The token runs (first token, tokens) of some bands in token order: every
+// (frame, line range) of the bands, sorted, adjacent ones merged -- so the
+// bands of one frame slab that cover all its lines become a single run.
 std::vector<std::pair<int64_t, int64_t>> band_runs(const Split& s, const awa_plan_info& info, const int* bands, int n)
 {
-    std::vector<std::pair<int64_t, int64_t>> runs;
+    std::vector<std::pair<int64_t, int64_t>> pieces;
     const int64_t line = info.source_w;
     for (int i = 0; i < n; i++)
     {
         const Band& b = s.bands[bands[i]];
         for (int t = b.t0; t < b.t1; t++)
-        {
-            const int64_t first = ((int64_t)t * info.source_h + b.h0) * line, count = (int64_t)(b.h1 - b.h0) * line;
-            if (!runs.empty() && runs.back().first + runs.back().second == first)
-                runs.back().second += count;
-            else
-                runs.emplace_back(first, count);
-        }
+            pieces.emplace_back(((int64_t)t * info.source_h + b.h0) * line, (int64_t)(b.h1 - b.h0) * line);
     }
+    std::sort(pieces.begin(), pieces.end());
+    std::vector<std::pair<int64_t, int64_t>> runs;
+    for (const auto& p : pieces)
+        if (!runs.empty() && runs.back().first + runs.back().second == p.first)
+            runs.back().second += p.second;
+        else
+            runs.push_back(p);
     return runs;
 }
 
@@ -334,7 +337,7 @@ int barrier(const Nccl* n, awa_comm* c, cudaStream_t stream)
 }
 
 // ---------------------------------------------------------------- direct mode pushes
-constexpr int kPushChunks = 4;  // attention launches per rank, each followed by its rows' peer copies
+constexpr int kPushChunks = 3;  // attention launches per rank, each followed by its rows' peer copies
 
 // The side stream and events of the peer copies (made once per communicator).
 int push_streams(awa_comm* c)
@@ -347,8 +350,10 @@ int push_streams(awa_comm* c)
     return cuda_status(e, "peer copy stream");
 }
 
-// The rank's bands cut into at most kPushChunks runs of near-equal cost:
-// returns the band-list offsets of the cuts (first 0, last the band count).
+// The rank's bands cut into at most kPushChunks runs: returns the band-list
+// offsets of the cuts (first 0, last the band count). The chunk costs shrink
+// geometrically (halving), since only the last chunk's copies are not hidden
+// behind a later chunk's attention.
 std::vector<int> push_chunks(const Split& s, int rank)
 {
     const auto& rb = s.rank_bands[rank];
@@ -356,13 +361,21 @@ std::vector<int> push_chunks(const Split& s, int rank)
     for (int b : rb)
         total += s.bands[b].cost;
     const int chunks = std::max(1, std::min<int>(kPushChunks, (int)rb.size()));
+    // shares 2^(chunks-1) : ... : 2 : 1 of the cost, cumulative targets
+    std::vector<double> target;
+    double sum = 0, unit = total / ((1 << chunks) - 1);
+    for (int c = 0; c < chunks - 1; c++)
+    {
+        sum += unit * (1 << (chunks - 1 - c));
+        target.push_back(sum);
+    }
     std::vector<int> cuts{0};
     double acc = 0;
     for (size_t i = 0; i < rb.size(); i++)
     {
         acc += s.bands[rb[i]].cost;
-        const int c = (int)cuts.size();
-        if (c < chunks && i + 1 < rb.size() && acc >= total * c / chunks)
+        const size_t c = cuts.size() - 1;
+        if (c < target.size() && i + 1 < rb.size() && acc >= target[c])
             cuts.push_back((int)i + 1);
     }
     cuts.push_back((int)rb.size());
@@ -847,7 +860,7 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
                                           comm->comm, st),
                          "ncclAllReduce (text partial sums)");
     if (rc == AWA_OK)
-        rc = nccl_status(n, n->all_gather(gather + r * slot_bytes, gather, slot_bytes, ncclUint8, comm->comm, st),
+        rc = nccl_status(n, n->all_gather(gather + r * slot_bytes, gather, slot_bytes / osz, otype, comm->comm, st),
                          "ncclAllGather (video rows)");
     const int end_rc = nccl_status(n, n->group_end(), "ncclGroupEnd");
     rc = rc ? rc : end_rc;
