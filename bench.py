@@ -63,6 +63,10 @@ WORKLOADS = {
                     "in the workspace, then the tensor-core kernel"),
 }
 INPUT_F32 = {"cfg4-f32qkv"}  # workloads whose QKV rows are fp32 although the block is bf16
+WORKLOADS["cfg4-prerotated"] = ((21, 64, 64), (6, 8, 8), 0, "bf16",
+                                "cfg4 with Q/K rotated by the QKV projection's epilogue "
+                                "(awa_qkv_project_rotated): awa_forward_prerotated, no rotation in the attention")
+PREROTATED = {"cfg4-prerotated"}
 
 
 def window_costs(grid, num, shifted):
@@ -477,9 +481,11 @@ def run_b200(args, rank, world, local_rank):
     workspace = torch.empty(plan.workspace_bytes(HEADS, HEAD_DIM, prec, in_dtype), device=device, dtype=torch.uint8)
     stream = torch.cuda.current_stream(device)
 
+    forward = plan.forward_prerotated if name in PREROTATED else plan.forward
+
     def step():
-        plan.forward(video_qkv, text_qkv, prec, out_dtype=dtype, workspace=workspace, video_out=video_out,
-                     text_out=text_out, stream=stream)
+        forward(video_qkv, text_qkv, prec, out_dtype=dtype, workspace=workspace, video_out=video_out,
+                text_out=text_out, stream=stream)
 
     def barrier():
         if world > 1:
