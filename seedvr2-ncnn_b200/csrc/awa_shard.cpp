@@ -138,8 +138,12 @@ struct awa_comm
     bool owned = false;
     std::vector<SharedBuffer> shared;
     int* barrier_word = nullptr;  // device int for the entry barrier of the direct mode
-    cudaStream_t push_stream = nullptr;  // direct mode: peer copies of video rows
-    cudaEvent_t push_events[8] = {};     // per chunk, and the join
+    // direct mode: the peer copies of video rows, one stream per peer (copies
+    // to different peers run on different copy engines at once), the events
+    // that start a chunk's copies and those that join them back
+    std::vector<cudaStream_t> push_stream;
+    cudaEvent_t chunk_ready[8] = {};
+    std::vector<cudaEvent_t> push_done;
 };
 
 namespace
@@ -339,15 +343,25 @@ int barrier(const Nccl* n, awa_comm* c, cudaStream_t stream)
 // ---------------------------------------------------------------- direct mode pushes
 constexpr int kPushChunks = 3;  // attention launches per rank, each followed by its rows' peer copies
 
-// The side stream and events of the peer copies (made once per communicator).
+// The peer-copy streams and events (made once per communicator).
 int push_streams(awa_comm* c)
 {
-    if (c->push_stream)
+    if (!c->push_stream.empty())
         return AWA_OK;
-    cudaError_t e = cudaStreamCreateWithFlags(&c->push_stream, cudaStreamNonBlocking);
-    for (int i = 0; i < kPushChunks + 1 && e == cudaSuccess; i++)
-        e = cudaEventCreateWithFlags(&c->push_events[i], cudaEventDisableTiming);
-    return cuda_status(e, "peer copy stream");
+    cudaError_t e = cudaSuccess;
+    for (int q = 0; q < c->nranks - 1 && e == cudaSuccess; q++)
+    {
+        cudaStream_t s = nullptr;
+        cudaEvent_t d = nullptr;
+        e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+        if (e == cudaSuccess)
+            e = cudaEventCreateWithFlags(&d, cudaEventDisableTiming);
+        c->push_stream.push_back(s);
+        c->push_done.push_back(d);
+    }
+    for (int i = 0; i < kPushChunks && e == cudaSuccess; i++)
+        e = cudaEventCreateWithFlags(&c->chunk_ready[i], cudaEventDisableTiming);
+    return cuda_status(e, "peer copy streams");
 }
 
 // The rank's bands cut into at most kPushChunks runs: returns the band-list
@@ -383,22 +397,24 @@ std::vector<int> push_chunks(const Split& s, int rank)
 }
 
 // Copies token runs of video rows from `local` into every peer at the same
-// offsets, on the side stream once the work enqueued so far on `st` is done.
-// A run is one contiguous byte range (its tokens' rows and the padding between
-// them), so each goes as a single peer copy.
+// offsets, once the work enqueued so far on `st` is done: each peer's copies on
+// its own stream. A run is one contiguous byte range (its tokens' rows and the
+// padding between them), so each goes as a single peer copy.
 int push_runs(awa_comm* c, const std::vector<std::pair<int64_t, int64_t>>& runs, unsigned char* local,
               const std::vector<unsigned char*>& peers, int64_t token_bytes, int64_t row_bytes, size_t chunk,
               cudaStream_t st)
 {
-    cudaError_t e = cudaEventRecord(c->push_events[chunk], st);
-    if (e == cudaSuccess)
-        e = cudaStreamWaitEvent(c->push_stream, c->push_events[chunk], 0);
-    for (const auto& run : runs)
+    cudaError_t e = cudaEventRecord(c->chunk_ready[chunk], st);
+    for (size_t q = 0; q < peers.size() && e == cudaSuccess; q++)
     {
-        const int64_t off = run.first * token_bytes, bytes = (run.second - 1) * token_bytes + row_bytes;
-        for (unsigned char* peer : peers)
+        e = cudaStreamWaitEvent(c->push_stream[q], c->chunk_ready[chunk], 0);
+        for (const auto& run : runs)
+        {
+            const int64_t off = run.first * token_bytes, bytes = (run.second - 1) * token_bytes + row_bytes;
             if (e == cudaSuccess)
-                e = cudaMemcpyAsync(peer + off, local + off, (size_t)bytes, cudaMemcpyDeviceToDevice, c->push_stream);
+                e = cudaMemcpyAsync(peers[q] + off, local + off, (size_t)bytes, cudaMemcpyDeviceToDevice,
+                                    c->push_stream[q]);
+        }
     }
     return cuda_status(e, "peer copy of video rows");
 }
@@ -406,9 +422,13 @@ int push_runs(awa_comm* c, const std::vector<std::pair<int64_t, int64_t>>& runs,
 // `st` waits for every peer copy issued so far.
 int join_pushes(awa_comm* c, cudaStream_t st)
 {
-    cudaError_t e = cudaEventRecord(c->push_events[kPushChunks], c->push_stream);
-    if (e == cudaSuccess)
-        e = cudaStreamWaitEvent(st, c->push_events[kPushChunks], 0);
+    cudaError_t e = cudaSuccess;
+    for (size_t q = 0; q < c->push_stream.size() && e == cudaSuccess; q++)
+    {
+        e = cudaEventRecord(c->push_done[q], c->push_stream[q]);
+        if (e == cudaSuccess)
+            e = cudaStreamWaitEvent(st, c->push_done[q], 0);
+    }
     return cuda_status(e, "peer copy join");
 }
 
@@ -589,11 +609,15 @@ void awa_comm_destroy(awa_comm* comm)
         release_shared(b, comm->rank);
     if (comm->barrier_word)
         cudaFree(comm->barrier_word);
-    for (cudaEvent_t e : comm->push_events)
+    for (cudaEvent_t e : comm->chunk_ready)
         if (e)
             cudaEventDestroy(e);
-    if (comm->push_stream)
-        cudaStreamDestroy(comm->push_stream);
+    for (cudaEvent_t e : comm->push_done)
+        if (e)
+            cudaEventDestroy(e);
+    for (cudaStream_t s : comm->push_stream)
+        if (s)
+            cudaStreamDestroy(s);
     const Nccl* n = nccl();
     if (comm->owned && comm->comm && n)
         n->comm_destroy(comm->comm);
