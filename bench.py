@@ -429,8 +429,9 @@ def run_sharded(args, rank, world, local_rank):
             "config": workload_config(name, world, "sharded"),
             "windows": W, "attn_tflops": round(flops / (ms_per_step / 1000.0) / 1e12, 2),
             "sharded": {"split": "heads" if by_heads else "windows", "bounds": bounds,
-                        "exchange": ("video rows stored by the attention kernel into every rank's output over NVLink "
-                                     "(P2P); NCCL all-reduce of the text partial sums" if direct else
+                        "exchange": ("video rows pushed by peer copies (copy engines, one stream per peer) into every "
+                                     "rank's output in a buffer shared over the ranks, chunk by chunk behind the "
+                                     "attention; NCCL all-reduce of the text partial sums" if direct else
                                      "NCCL all-gather of the video rows, all-reduce of the text partial sums"),
                         "compute_ms_max": round(compute_ms_max, 5),
                         "collective_and_copies_ms": round(ms_per_step - compute_ms_max, 5),
@@ -649,7 +650,8 @@ def run_qkv_proj(args, rank, world, local_rank):
     torch.cuda.set_device(device)
     grid = WORKLOADS[args.workload][0]
     n_v = grid[0] * grid[1] * grid[2]
-    producer = args.stage == "qkv-proj"
+    producer = args.stage in ("qkv-proj", "qkv-proj-rope")
+    rotated = args.stage == "qkv-proj-rope"
     n_out = 3 * HEADS * HEAD_DIM if producer else MODEL_DIM
     gen = torch.Generator(device=device).manual_seed(4321 + rank)
     x = torch.randn(n_v, MODEL_DIM, device=device, generator=gen).bfloat16()
@@ -660,8 +662,16 @@ def run_qkv_proj(args, rank, world, local_rank):
         gk = 1.0 + 0.25 * torch.randn(HEAD_DIM, device=device, generator=gen)
         out = torch.empty(n_v, 3, HEADS, HEAD_DIM, device=device, dtype=torch.bfloat16)
 
-        def step():
-            awa_b200.qkv_project(x, w, gq, gk, 1e-5, HEADS, out=out, stream=stream)
+        if rotated:
+            _, num, shifted, _, _ = WORKLOADS[args.workload]
+            plan = awa_b200.AwaPlan(*grid, *num, text_tokens=TEXT, shifted=bool(shifted))
+
+            def step():
+                awa_b200.qkv_project_rotated(x, w, gq, gk, 1e-5, HEADS, plan, awa_b200.AWA_BRANCH_VIDEO, out=out,
+                                             stream=stream)
+        else:
+            def step():
+                awa_b200.qkv_project(x, w, gq, gk, 1e-5, HEADS, out=out, stream=stream)
     else:
         bias = 0.1 * torch.randn(n_out, device=device, generator=gen)
         gate = 0.2 * torch.randn(n_out, device=device, generator=gen)
@@ -701,7 +711,7 @@ def run_qkv_proj(args, rank, world, local_rank):
     ms_per_step = float(t.item()) / args.steps
     awa_b200.device_status()
     flops = 2.0 * n_v * MODEL_DIM * n_out
-    kernel_name = "awa_qkv_project" if producer else "awa_out_project"
+    kernel_name = ("awa_qkv_project_rotated" if rotated else "awa_qkv_project") if producer else "awa_out_project"
     launches, kernel_total = prof.get(kernel_name, (0, 0.0))
     kernel_ms = kernel_total / max(launches, 1)
     peaks = {}
@@ -728,7 +738,8 @@ def run_qkv_proj(args, rank, world, local_rank):
     torch.cuda.synchronize()
     gemm_ms = g0.elapsed_time(g1) / args.steps
     return {
-        "metric": ("QKV projection + per-head RMSNorm (producer of the AWA input)" if producer else
+        "metric": (("QKV projection + per-head RMSNorm + MMRoPE (producer of the pre-rotated AWA input)" if rotated
+                    else "QKV projection + per-head RMSNorm (producer of the AWA input)") if producer else
                    "proj_out + Ada gate + residual (consumer of the AWA output)") + " TFLOP/s per B200",
         "value": round(flops * world / (ms_per_step / 1000.0) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
@@ -994,7 +1005,8 @@ def main():
                              "replicas runs an independent layer per GPU (weak scaling)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiler captures)")
-    parser.add_argument("--stage", default="awa", choices=["awa", "qkv-proj", "out-proj", "stack", "layers"],
+    parser.add_argument("--stage", default="awa",
+                        choices=["awa", "qkv-proj", "qkv-proj-rope", "out-proj", "stack", "layers"],
                         help="awa: the AWA layer (the headline); qkv-proj / out-proj: its input's producer / "
                              "its output's consumer; stack: the attention path of 32 blocks via the stack driver; layers: "
                              "the four layers as separate passes, per-kernel HBM throughput")
@@ -1021,7 +1033,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.stage in ("qkv-proj", "out-proj", "stack", "layers"):
+        if args.stage in ("qkv-proj", "qkv-proj-rope", "out-proj", "stack", "layers"):
             runner = {"stack": run_stack, "layers": run_layers}.get(args.stage, run_qkv_proj)
             line = runner(args, rank, world, local_rank)
             if rank == 0:
