@@ -310,6 +310,8 @@ def run_sharded(args, rank, world, local_rank):
     box = [awa_b200.AwaComm.unique_id() if rank == 0 else None]
     dist.broadcast_object_list(box, src=0)
     comm = awa_b200.AwaComm(box[0], world, rank)
+    comm.set_push({"auto": awa_b200.AWA_PUSH_AUTO, "ce": awa_b200.AWA_PUSH_COPY_ENGINES,
+                   "kernel": awa_b200.AWA_PUSH_KERNEL}[args.push])
     by_heads, bounds = plan.shard_split(world, HEADS)
 
     gen = torch.Generator(device=device).manual_seed(1234)  # the same layer on every rank
@@ -429,9 +431,10 @@ def run_sharded(args, rank, world, local_rank):
             "config": workload_config(name, world, "sharded"),
             "windows": W, "attn_tflops": round(flops / (ms_per_step / 1000.0) / 1e12, 2),
             "sharded": {"split": "heads" if by_heads else "windows", "bounds": bounds,
-                        "exchange": ("video rows pushed by peer copies (copy engines, one stream per peer) into every "
-                                     "rank's output in a buffer shared over the ranks, chunk by chunk behind the "
-                                     "attention; NCCL all-reduce of the text partial sums" if direct else
+                        "exchange": ("video rows pushed into every rank's output in a buffer shared over the ranks "
+                                     f"(push {args.push}: copy engines chunk by chunk behind the attention with one "
+                                     "peer, the SM push kernel after it with three or more); NCCL all-reduce of the "
+                                     "text partial sums" if direct else
                                      "NCCL all-gather of the video rows, all-reduce of the text partial sums"),
                         "compute_ms_max": round(compute_ms_max, 5),
                         "collective_and_copies_ms": round(ms_per_step - compute_ms_max, 5),
@@ -997,6 +1000,8 @@ def main():
     parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
     parser.add_argument("--workload", default="cfg4", choices=sorted(WORKLOADS))
     parser.add_argument("--e2e-steps", type=int, default=20)
+    parser.add_argument("--push", default="auto", choices=["auto", "ce", "kernel"],
+                        help="p2p exchange: copy engines (ce), the SM push kernel, or auto (ce with one peer)")
     parser.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                         help="sharded mode: p2p = the attention kernel stores video rows into every rank's output "
                              "(shared buffer); nccl = NCCL all-gather of the rows")

@@ -298,6 +298,16 @@ void awa_comm_destroy(awa_comm* comm);
 int awa_comm_alloc_shared(awa_comm* comm, size_t bytes, void** ptr);
 /* Collective: waits for every rank, unmaps and frees a shared buffer. */
 int awa_comm_free_shared(awa_comm* comm, void* ptr);
+/* How the direct mode moves a rank's video rows into the peers' copies:
+ * AWA_PUSH_COPY_ENGINES -- one cudaMemcpyAsync per token run and peer on the
+ * copy engines (one stream per peer), chunk by chunk behind the attention;
+ * AWA_PUSH_KERNEL -- after one attention launch, an SM kernel loads each run
+ * once and stores it into every peer over NVLink; AWA_PUSH_AUTO (default) --
+ * the copy engines with one peer, the kernel with three or more. */
+#define AWA_PUSH_AUTO 0
+#define AWA_PUSH_COPY_ENGINES 1
+#define AWA_PUSH_KERNEL 2
+int awa_comm_set_push(awa_comm* comm, int mode);
 int awa_comm_info(const awa_comm* comm, int* rank, int* nranks);
 /* The split awa_forward_sharded uses for nranks ranks: *by_heads (0/1) and
  * nranks+1 bounds: head indices for a head split; for a window split the

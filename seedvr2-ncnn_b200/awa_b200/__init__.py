@@ -34,6 +34,9 @@ AWA_ERR_ALLOC = -100
 AWA_NOALLOC_SCRATCH_BYTES = 32 << 20  # scratch of awa_forward_noalloc, per GPU
 AWA_BRANCH_VIDEO = 0
 AWA_BRANCH_TEXT = 1
+AWA_PUSH_AUTO = 0
+AWA_PUSH_COPY_ENGINES = 1
+AWA_PUSH_KERNEL = 2
 
 # Every symbol declared in include/awa_b200.h, include/awa_package.h and include/awa_stack.h.
 EXPORTED_SYMBOLS = (
@@ -46,7 +49,7 @@ EXPORTED_SYMBOLS = (
     "awa_window_range_video_rows", "awa_partition_windows", "awa_qkv_project", "awa_out_project", "awa_device_status",
     "awa_selftest_bounded_wait", "awa_attention_kernel_kind",
     "awa_comm_unique_id", "awa_comm_create", "awa_comm_wrap", "awa_comm_destroy", "awa_comm_info", "awa_shard_split",
-    "awa_comm_alloc_shared", "awa_comm_free_shared", "awa_shard_windows",
+    "awa_comm_alloc_shared", "awa_comm_free_shared", "awa_shard_windows", "awa_comm_set_push",
     "awa_forward_sharded_workspace_bytes", "awa_forward_sharded",
     "awa_profile_enable", "awa_profile_reset", "awa_profile_collect", "awa_last_error", "awa_version",
     "awa_graph_find_chains", "awa_graph_find_chains_file", "awa_graph_make_dynamic", "awa_manifest_validate",
@@ -149,6 +152,7 @@ def library() -> ctypes.CDLL:
         "awa_comm_destroy": (None, [p]),
         "awa_comm_alloc_shared": (i, [p, sz, ctypes.POINTER(p)]),
         "awa_comm_free_shared": (i, [p, p]),
+        "awa_comm_set_push": (i, [p, i]),
         "awa_comm_info": (i, [p, ctypes.POINTER(i), ctypes.POINTER(i)]),
         "awa_shard_split": (i, [p, i, i, ctypes.POINTER(i), p]),
         "awa_shard_windows": (i, [p, i, i, i, p, i]),
@@ -689,6 +693,10 @@ class AwaComm:
     @property
     def handle(self):
         return self._handle
+
+    def set_push(self, mode: int) -> None:
+        """How the direct mode moves video rows (AWA_PUSH_AUTO / _COPY_ENGINES / _KERNEL)."""
+        _check(library().awa_comm_set_push(self._handle, mode))
 
     def shared_tensor(self, shape, dtype):
         """Collective: a torch tensor over a buffer shared by every rank

@@ -643,6 +643,26 @@ int launch_text_scale(int rows, int heads, int head_dim, const float* text_sum, 
     return (int)cudaGetLastError();
 }
 
+// Byte runs of this GPU's buffer pushed into the same offsets of peer
+// buffers over NVLink (plain 16-byte loads here, 16-byte stores there):
+// blockIdx.y picks the run, the threads stride through it. Every thread
+// fences at system scope before it ends, so the collective the host enqueues
+// next orders the stores before the peers' reads.
+__global__ void __launch_bounds__(256) push_runs_kernel(const uint4* __restrict__ local, PushPeers peers,
+                                                        PushRuns runs)
+{
+    const int r = blockIdx.y;
+    const int64_t first = runs.first[r], count = runs.count[r];
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
+    {
+        const uint4 v = __ldg(local + first + i);
+#pragma unroll 1
+        for (int q = 0; q < peers.count; q++)
+            peers.ptr[q][first + i] = v;
+    }
+    __threadfence_system();
+}
+
 int launch_rows_to_bf16(const void* src, int64_t ts, int64_t qs, int tokens, int64_t row, void* dst,
                         cudaStream_t stream)
 {
@@ -657,6 +677,21 @@ int launch_rows_to_bf16(const void* src, int64_t ts, int64_t qs, int tokens, int
         rows_to_bf16_kernel<true><<<grid, 256, 0, stream>>>((const float*)src, ts, qs, tokens, (int)row, (uint4*)dst);
     else
         rows_to_bf16_kernel<false><<<grid, 256, 0, stream>>>((const float*)src, ts, qs, tokens, (int)row, (uint4*)dst);
+    return (int)cudaGetLastError();
+}
+
+int launch_push_runs(const void* local, const PushPeers& peers, const PushRuns& runs, cudaStream_t stream)
+{
+    if (runs.n <= 0 || peers.count <= 0)
+        return 0;
+    if (runs.n > kMaxPushRuns || peers.count > kMaxPushPeers || reinterpret_cast<uintptr_t>(local) % 16)
+        return (int)cudaErrorInvalidValue;
+    int64_t most = 0;
+    for (int r = 0; r < runs.n; r++)
+        most = std::max<int64_t>(most, runs.count[r]);
+    ProfileScope prof("awa_push_runs", stream);
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((most + 255) / 256, 1184 / runs.n + 1));
+    push_runs_kernel<<<dim3(blocks, runs.n), 256, 0, stream>>>(static_cast<const uint4*>(local), peers, runs);
     return (int)cudaGetLastError();
 }
 

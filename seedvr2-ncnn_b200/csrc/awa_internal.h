@@ -127,6 +127,23 @@ int launch_text_scale(int rows, int heads, int head_dim, const float* text_sum, 
 // a multiple of 8) -> dense bf16 rows [tokens][3][row], round to nearest even.
 int launch_rows_to_bf16(const void* src, int64_t ts, int64_t qs, int tokens, int64_t row, void* dst,
                         cudaStream_t stream);
+// The peers and byte runs of one push (launch_push_runs), in 16-byte units.
+constexpr int kMaxPushPeers = 7;
+constexpr int kMaxPushRuns = 96;
+struct PushPeers
+{
+    uint4* ptr[kMaxPushPeers];
+    int count;
+};
+struct PushRuns
+{
+    int64_t first[kMaxPushRuns];  // first 16-byte unit of each run
+    int64_t count[kMaxPushRuns];  // units
+    int n;
+};
+// Copies the runs of `local` into every peer at the same offsets (SM loads
+// and NVLink stores), with a system-scope fence at the end of every thread.
+int launch_push_runs(const void* local, const PushPeers& peers, const PushRuns& runs, cudaStream_t stream);
 int launch_shard_copy(const PlanDevice& plan, int heads, int head_dim, int window_begin, int window_end, int dtype,
                       const void* src, int64_t src_stride, void* dst, int64_t dst_stride, int to_source,
                       cudaStream_t stream);

@@ -144,6 +144,7 @@ struct awa_comm
     std::vector<cudaStream_t> push_stream;
     cudaEvent_t chunk_ready[8] = {};
     std::vector<cudaEvent_t> push_done;
+    int push_mode = AWA_PUSH_AUTO;  // how direct mode moves the video rows
 };
 
 namespace
@@ -432,9 +433,42 @@ int join_pushes(awa_comm* c, cudaStream_t st)
     return cuda_status(e, "peer copy join");
 }
 
+// Pushes token runs into every peer with the SM copy kernel on `st` (after the
+// work enqueued there), in launches of at most kMaxPushRuns runs.
+int push_runs_kernel(const std::vector<std::pair<int64_t, int64_t>>& runs, unsigned char* local,
+                     const std::vector<unsigned char*>& peers, int64_t token_bytes, int64_t row_bytes, cudaStream_t st)
+{
+    awa::PushPeers pp{};
+    pp.count = (int)peers.size();
+    for (size_t q = 0; q < peers.size(); q++)
+        pp.ptr[q] = reinterpret_cast<uint4*>(peers[q]);
+    size_t i = 0;
+    while (i < runs.size())
+    {
+        awa::PushRuns pr{};
+        for (; i < runs.size() && pr.n < awa::kMaxPushRuns; i++, pr.n++)
+        {
+            pr.first[pr.n] = runs[i].first * token_bytes / 16;
+            pr.count[pr.n] = ((runs[i].second - 1) * token_bytes + row_bytes) / 16;
+        }
+        const int e = awa::launch_push_runs(local, pp, pr, st);
+        if (e)
+            return cuda_status(static_cast<cudaError_t>(e), "peer push kernel");
+    }
+    return AWA_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+int awa_comm_set_push(awa_comm* comm, int mode)
+{
+    if (!comm || (mode != AWA_PUSH_AUTO && mode != AWA_PUSH_COPY_ENGINES && mode != AWA_PUSH_KERNEL))
+        return fail(AWA_ERR_INVALID, "awa_comm_set_push: unknown mode %d", mode);
+    comm->push_mode = mode;
+    return AWA_OK;
+}
 
 int awa_comm_alloc_shared(awa_comm* comm, size_t bytes, void** out)
 {
@@ -809,10 +843,38 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
     const size_t partial_bytes = l.gather - l.forward;
     const size_t window_partial = (size_t)info.text_tokens * row;  // elements per window
     int partial_dtype = AWA_F32;
+    const int64_t rank_units_ok = tbytes % 16 == 0 && rbytes % 16 == 0 &&
+                                  reinterpret_cast<uintptr_t>(video_out) % 16 == 0;
+    const bool push_kernel = direct && rank_units_ok &&
+                             (comm->push_mode == AWA_PUSH_KERNEL ||
+                              (comm->push_mode == AWA_PUSH_AUTO && (int)peers.size() >= 3));
+    if (direct && push_kernel)
+    {
+        // one attention launch over the rank's windows, then the SM copy kernel
+        // pushes its rows into every peer (NVLink stores from all SMs)
+        const auto& rb = s.rank_bands[r];
+        rc = awa::attention_set(plan, precision, heads, head_dim, mine.data(), (int)mine.size(), in_dtype, video_qkv,
+                                video_token_stride, video_qkv_stride, text_qkv, text_token_stride, text_qkv_stride,
+                                out_dtype, video_out, video_token_stride_out, partials, partial_bytes, &partial_dtype,
+                                st);
+        if (rc == AWA_OK)
+            rc = push_runs_kernel(band_runs(s, info, rb.data(), (int)rb.size()), static_cast<unsigned char*>(video_out),
+                                  peers, tbytes, rbytes, st);
+        if (rc == AWA_OK)
+            rc = awa::text_partial_sum(plan, heads, head_dim, partial_dtype, partials, 0, (int)mine.size(), text_sum,
+                                       st);
+        if (rc == AWA_OK)
+            rc = nccl_status(n, n->all_reduce(text_sum, text_sum, (size_t)info.text_tokens * row, ncclFloat32, ncclSum,
+                                              comm->comm, st),
+                             "ncclAllReduce (text partial sums)");
+        if (rc)
+            return rc;
+        return awa_text_finalize(plan, heads, head_dim, text_sum, out_dtype, text_out, text_token_stride_out, stream);
+    }
     if (direct)
     {
         // chunk by chunk: attention of the chunk's windows, then its rows to the
-        // peers on the side stream while the next chunk computes
+        // peers on the copy engines while the next chunk computes
         const std::vector<int> cuts = push_chunks(s, r);
         const auto& rb = s.rank_bands[r];
         const size_t psz = awa_attention_kernel_kind(plan, precision, in_dtype, heads, head_dim) == 1 ? 2 : 4;

@@ -65,15 +65,22 @@ def main(rank: int, world: int, port: int, out_path: str) -> None:
         video_s, text_s = plan.forward_sharded(comm, v, t, prec, out_dtype=torch.float32)
         video_b, text_b = plan.forward_sharded(comm, v, t, prec, out_dtype=dtype)  # outputs in the block dtype
         video_1, text_1 = plan.forward(v, t, prec, out_dtype=torch.float32)
-        # direct mode: the video output in a buffer shared over the ranks, rows
-        # stored straight into every rank's copy by the tensor-core kernel
+        # direct mode: the video output in a buffer shared over the ranks, each
+        # rank's rows pushed into every rank's copy -- by the copy engines and by
+        # the SM push kernel
+        direct_equal, direct_text_rel = True, 0.0
         shared = comm.shared_tensor((cfg.source_tokens, cfg.heads, cfg.head_dim), torch.float32)
-        shared.fill_(float("nan"))
-        torch.cuda.synchronize()
-        video_d, text_d = plan.forward_sharded(comm, v, t, prec, out_dtype=torch.float32, video_out=shared)
-        torch.cuda.synchronize()
-        direct_equal = bool(torch.equal(video_d, video_1))
-        direct_text_rel = rel_l2(text_d.cpu().numpy(), text_1.cpu().numpy())
+        for mode in (awa_b200.AWA_PUSH_COPY_ENGINES, awa_b200.AWA_PUSH_KERNEL):
+            comm.set_push(mode)
+            shared.fill_(float("nan"))
+            torch.cuda.synchronize()
+            dist.barrier()
+            video_d, text_d = plan.forward_sharded(comm, v, t, prec, out_dtype=torch.float32, video_out=shared)
+            torch.cuda.synchronize()
+            direct_equal = direct_equal and bool(torch.equal(video_d, video_1))
+            direct_text_rel = max(direct_text_rel, rel_l2(text_d.cpu().numpy(), text_1.cpu().numpy()))
+            dist.barrier()
+        comm.set_push(awa_b200.AWA_PUSH_AUTO)
         comm.free_shared(shared)
         torch.cuda.synchronize()
         status = 0
