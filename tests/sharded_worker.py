@@ -1,9 +1,10 @@
 """One rank of the multi-GPU parity test (tests/test_gpu_sharded.py).
 
-Run as `python tests/sharded_worker.py RANK WORLD PORT OUT_JSON`, one process
-per GPU. Each rank builds the same seeded inputs, runs awa_forward_sharded over
-an NCCL communicator (awa_comm_create, id handed out over a gloo process group
-on 127.0.0.1) and the single-GPU awa_forward on its own GPU, and writes what it
+Run as `python tests/sharded_worker.py RANK WORLD STORE_FILE OUT_JSON`, one
+process per GPU. Each rank builds the same seeded inputs, runs
+awa_forward_sharded over an NCCL communicator (awa_comm_create, id handed out
+over a gloo process group that meets through STORE_FILE, so no port can be
+taken) and the single-GPU awa_forward on its own GPU, and writes what it
 observed to OUT_JSON. Every rank takes the same collective steps whatever its
 checks find; the test asserts on the JSON files.
 """
@@ -40,9 +41,9 @@ CASES = [
 ]
 
 
-def main(rank: int, world: int, port: int, out_path: str) -> None:
+def main(rank: int, world: int, store_file: str, out_path: str) -> None:
     torch.cuda.set_device(rank)
-    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+    dist.init_process_group("gloo", init_method=f"file://{store_file}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60))
     box = [awa_b200.AwaComm.unique_id() if rank == 0 else None]
     dist.broadcast_object_list(box, src=0)
@@ -109,4 +110,4 @@ def main(rank: int, world: int, port: int, out_path: str) -> None:
 
 
 if __name__ == "__main__":
-    main(int(sys.argv[1]), int(sys.argv[2]), int(sys.argv[3]), sys.argv[4])
+    main(int(sys.argv[1]), int(sys.argv[2]), sys.argv[3], sys.argv[4])

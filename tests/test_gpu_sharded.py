@@ -16,7 +16,6 @@ rank's copy over NVLink.
 
 import json
 import os
-import socket
 import subprocess
 import sys
 
@@ -34,18 +33,12 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 WORLD = 2
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
 @pytest.fixture(scope="module")
 def rank_results(tmp_path_factory):
     out = tmp_path_factory.mktemp("sharded")
-    port = _free_port()
+    store = out / "rendezvous"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "sharded_worker.py"), str(r), str(WORLD), str(port),
+    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "sharded_worker.py"), str(r), str(WORLD), str(store),
                                str(out / f"rank{r}.json")], env=env) for r in range(WORLD)]
     codes = []
     for p in procs:
