@@ -1,26 +1,29 @@
 // awa_shard.cpp -- one AWA layer split over the GPUs of a node
-// (include/awa_b200.h: awa_comm_*, awa_forward_sharded).
+// (include/awa_b200.h: awa_comm_*, awa_shard_*, awa_forward_sharded).
 //
 // Windows are independent (SeedVR2WindowAttention::forward runs each window on
 // its own, awa_layers.cpp:1062-1120); the only coupling between them is the
 // text mean text[i] = sum_w attended_text(w)[i] / W (awa_layers.cpp:684-685).
-// So each rank computes a share of the layer and two collectives finish it:
+// So each rank computes a share of the layer and the ranks exchange the rest:
 //
-//   window split (enough windows): rank r runs the fused forward on a
-//     contiguous range of windows of near-equal attention cost, packs its
-//     video rows into its slot of a gather buffer, NCCL all-gathers the slots
-//     (in place), all-reduces the fp32 text partial sums and scatters the other
-//     ranks' rows into its own video output;
-//   head split (fewer than 4 windows per rank): rank r runs the whole layer for
-//     a range of heads -- the QKV and output pointers offset by the first head,
-//     the row strides unchanged -- and the all-gather moves head slices of the
-//     video and text outputs.
+//   window split: the windows sharing a (t-range, h-range) form a band
+//     (frames x whole grid lines); bands in (t, h) order are cut into one run
+//     of near-equal cost per rank, so a rank's video rows are a few contiguous
+//     token runs. The fp32 text partial sums are NCCL all-reduced. The video
+//     runs go to every rank's output: pushed straight into the other ranks'
+//     copies when video_out lies in a buffer shared over the ranks
+//     (awa_comm_alloc_shared: CUDA IPC), by the copy engines behind the
+//     attention or by an SM push kernel after it; else packed, NCCL
+//     all-gathered and copied back into place;
+//   head split (few bands or windows): rank r runs the whole layer for a range
+//     of heads -- the QKV and output pointers offset by the first head, the
+//     row strides unchanged -- and the head slices are exchanged.
 //
 // Every rank ends with the full video and text outputs, as the ncnn boundary
-// requires. NCCL moves the data into local memory: no kernel reads a peer's
-// memory and nothing uses TMA multicast. libnccl.so.2 is opened at run time,
-// so the library loads on machines without NCCL; inside a PyTorch process the
-// dynamic loader hands back the NCCL that torch already loaded.
+// requires. No attention kernel touches a peer's memory and nothing uses TMA
+// multicast; libnccl.so.2 is opened at run time, so the library loads on
+// machines without NCCL, and inside a PyTorch process the dynamic loader hands
+// back the NCCL that torch already loaded.
 #include "awa_b200.h"
 #include "awa_internal.h"
 
