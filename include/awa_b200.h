@@ -288,12 +288,12 @@ int awa_comm_wrap(void* nccl_comm, awa_comm** out);
 /* Frees any shared buffer still held (without the barrier of
  * awa_comm_free_shared) and the communicator. */
 void awa_comm_destroy(awa_comm* comm);
-/* Collective: a device buffer of `bytes` on every rank, each mapped into every
- * other rank's address space (CUDA IPC over NVLink). When video_out of
- * awa_forward_sharded lies in such a buffer and the tensor-core kernel runs,
- * the kernel stores each video row straight into every rank's copy (P2P stores
- * overlapping the attention; no all-gather, staging or scatter of the video
- * rows), behind an entry barrier so no rank overwrites rows another still
+/* Collective: a device buffer of `bytes` (the same on every rank, else
+ * AWA_ERR_INVALID) on every rank, each mapped into every other rank's address
+ * space (CUDA IPC over NVLink). When video_out of awa_forward_sharded lies in
+ * such a buffer -- at the same offset on every rank -- each rank's video rows
+ * are pushed straight into every other rank's copy (no all-gather, staging or
+ * scatter), behind an entry barrier so no rank overwrites rows another still
  * reads. *ptr is the local buffer (zeroed). */
 int awa_comm_alloc_shared(awa_comm* comm, size_t bytes, void** ptr);
 /* Collective: waits for every rank, unmaps and frees a shared buffer. */

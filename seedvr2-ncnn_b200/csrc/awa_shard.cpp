@@ -482,35 +482,46 @@ int awa_comm_alloc_shared(awa_comm* comm, size_t bytes, void** out)
     if (!n)
         return fail(AWA_ERR_CUDA, "awa_comm_alloc_shared: libnccl.so.2 could not be loaded");
     const int R = comm->nranks;
+    // what each rank publishes: its buffer's IPC handle and size (every rank's
+    // buffer must have the same size, since peers write at the writer's offsets)
+    struct Record
+    {
+        cudaIpcMemHandle_t handle;
+        uint64_t bytes;
+    };
     SharedBuffer b;
     b.bytes = bytes;
     b.peer.assign(R, nullptr);
-    unsigned char* handles = nullptr;
+    unsigned char* records = nullptr;
     cudaStream_t st = nullptr;
+    Record mine{};
+    mine.bytes = bytes;
     cudaError_t e = cudaMalloc(&b.local, bytes);
     if (e == cudaSuccess)
         e = cudaMemset(b.local, 0, bytes);
-    cudaIpcMemHandle_t mine;
     if (e == cudaSuccess)
-        e = cudaIpcGetMemHandle(&mine, b.local);
+        e = cudaIpcGetMemHandle(&mine.handle, b.local);
     if (e == cudaSuccess)
-        e = cudaMalloc(&handles, (size_t)R * sizeof(cudaIpcMemHandle_t));
+        e = cudaMalloc(&records, (size_t)R * sizeof(Record));
     if (e == cudaSuccess)
-        e = cudaMemcpy(handles + comm->rank * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice);
+        e = cudaMemcpy(records + comm->rank * sizeof(Record), &mine, sizeof(Record), cudaMemcpyHostToDevice);
     if (e == cudaSuccess)
         e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
     int rc = cuda_status(e, "awa_comm_alloc_shared");
-    // every rank's handle to every rank
     if (rc == AWA_OK)
-        rc = nccl_status(n, n->all_gather(handles + comm->rank * sizeof(mine), handles, sizeof(mine), ncclUint8,
+        rc = nccl_status(n, n->all_gather(records + comm->rank * sizeof(Record), records, sizeof(Record), ncclUint8,
                                           comm->comm, st),
                          "ncclAllGather (IPC handles)");
-    std::vector<cudaIpcMemHandle_t> all(R);
+    std::vector<Record> all(R);
     if (rc == AWA_OK)
         rc = cuda_status(cudaStreamSynchronize(st), "awa_comm_alloc_shared");
     if (rc == AWA_OK)
-        rc = cuda_status(cudaMemcpy(all.data(), handles, (size_t)R * sizeof(mine), cudaMemcpyDeviceToHost),
+        rc = cuda_status(cudaMemcpy(all.data(), records, (size_t)R * sizeof(Record), cudaMemcpyDeviceToHost),
                          "awa_comm_alloc_shared");
+    for (int q = 0; q < R && rc == AWA_OK; q++)
+        if (all[q].bytes != bytes)
+            rc = fail(AWA_ERR_INVALID, "awa_comm_alloc_shared: rank %d asked for %llu bytes, rank %d for %zu", q,
+                      (unsigned long long)all[q].bytes, comm->rank, bytes);
     for (int q = 0; q < R && rc == AWA_OK; q++)
     {
         if (q == comm->rank)
@@ -518,13 +529,13 @@ int awa_comm_alloc_shared(awa_comm* comm, size_t bytes, void** out)
             b.peer[q] = b.local;
             continue;
         }
-        rc = cuda_status(cudaIpcOpenMemHandle(&b.peer[q], all[q], cudaIpcMemLazyEnablePeerAccess),
+        rc = cuda_status(cudaIpcOpenMemHandle(&b.peer[q], all[q].handle, cudaIpcMemLazyEnablePeerAccess),
                          "cudaIpcOpenMemHandle");
     }
     if (st)
         cudaStreamDestroy(st);
-    if (handles)
-        cudaFree(handles);
+    if (records)
+        cudaFree(records);
     if (rc != AWA_OK)
     {
         release_shared(b, comm->rank);
