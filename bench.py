@@ -362,34 +362,46 @@ def run_sharded(args, rank, world, local_rank):
     compute_ms_max = float(t[1].item()) / args.steps
     value = W / (ms_per_step / 1000.0)
 
-    # end to end with host buffers: each rank copies its 1/N slice of the
-    # replicated QKV from pinned host memory, NCCL all-gathers the slices (every
-    # rank needs every row, as the ncnn boundary hands the layer whole inputs),
-    # runs the sharded layer, and copies its 1/N slice of the (replicated) video
-    # output back; rank 0 also copies the text output.
+    # end to end with host buffers: each rank copies from pinned host memory only
+    # the QKV rows its windows read (its bands' token runs, awa_shard_runs, and
+    # the text rows), runs the sharded layer, and copies its runs of the video
+    # output back; rank 0 also copies the text output. Together the ranks move
+    # the whole input in and the whole output out every step.
     e2e_ms, e2e_steps = None, 0
-    in_bytes = (n_v + TEXT) * 3 * HEADS * HEAD_DIM * esize
-    out_bytes = (n_v + TEXT) * HEADS * HEAD_DIM * esize
+    in_bytes = out_bytes = 0
     if not args.no_e2e:
         e2e_steps = max(3, min(args.steps, args.e2e_steps))
-        per = -(-n_v // world)
-        lo, hi = min(rank * per, n_v), min((rank + 1) * per, n_v)
-        host_v = torch.empty(per, 3, HEADS, HEAD_DIM, dtype=dtype, pin_memory=True)
-        host_v[: hi - lo].copy_(video_qkv[lo:hi])
+        runs = plan.shard_runs(world, HEADS, rank)
+        rows = sum(c for _, c in runs)
+        row_bytes = HEADS * HEAD_DIM * esize
+        # bytes copied per step, summed over the ranks
+        nb = torch.tensor([(rows + TEXT) * 3 * row_bytes, (rows + (TEXT if rank == 0 else 0)) * row_bytes],
+                          device=device, dtype=torch.float64)
+        dist.all_reduce(nb)
+        in_bytes, out_bytes = int(nb[0].item()), int(nb[1].item())
+        host_v = torch.empty(rows, 3, HEADS, HEAD_DIM, dtype=dtype, pin_memory=True)
+        host_o = torch.empty(rows, HEADS, HEAD_DIM, dtype=dtype, pin_memory=True)
+        at = 0
+        for first, count in runs:
+            host_v[at:at + count].copy_(video_qkv[first:first + count])
+            at += count
         host_t = torch.empty(text_qkv.shape, dtype=dtype, pin_memory=True)
         host_t.copy_(text_qkv)
-        host_o = torch.empty(per, HEADS, HEAD_DIM, dtype=dtype, pin_memory=True)
         host_ot = torch.empty(text_out.shape, dtype=dtype, pin_memory=True)
-        gathered = torch.empty(per * world, 3, HEADS, HEAD_DIM, dtype=dtype, device=device)
-        slot = torch.empty(per, 3, HEADS, HEAD_DIM, dtype=dtype, device=device)
+        dev_v = torch.zeros_like(video_qkv)
         dev_t = torch.empty_like(text_qkv)
 
         def e2e_step():
-            slot.copy_(host_v, non_blocking=True)
+            at = 0
+            for first, count in runs:
+                dev_v[first:first + count].copy_(host_v[at:at + count], non_blocking=True)
+                at += count
             dev_t.copy_(host_t, non_blocking=True)
-            dist.all_gather_into_tensor(gathered, slot)
-            step(gathered[:n_v], dev_t)
-            host_o[: hi - lo].copy_(video_out[lo:hi], non_blocking=True)
+            step(dev_v, dev_t)
+            at = 0
+            for first, count in runs:
+                host_o[at:at + count].copy_(video_out[first:first + count], non_blocking=True)
+                at += count
             if rank == 0:
                 host_ot.copy_(text_out, non_blocking=True)
 
@@ -443,8 +455,8 @@ def run_sharded(args, rank, world, local_rank):
             "e2e": None if e2e_ms is None else {
                 "value": round(W / (e2e_ms / 1000.0), 2), "unit": UNIT, "h2d_bytes_per_step": in_bytes,
                 "d2h_bytes_per_step": out_bytes, "steps": e2e_steps, "ms_per_step": round(e2e_ms, 4),
-                "how": "each rank copies 1/N of the QKV rows in and 1/N of the video rows out; NCCL all-gathers "
-                       "the input slices on the device"},
+                "how": "each rank copies in the QKV rows of its windows (its token runs + the text rows) and "
+                       "copies out its runs of the video output; rank 0 the text output"},
             "roofline": {"bound": "hbm", "kernel": attn_name, "achieved": round(achieved, 1), "peak": hbm_peak,
                          "unit": "GB/s", "frac": round(achieved / hbm_peak, 4), "traffic": None,
                          "peak_source": peak_src, "algorithmic_bytes": alg_bytes, "kernel_ms": round(attn_ms, 5),

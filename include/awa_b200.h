@@ -317,6 +317,13 @@ int awa_shard_split(const awa_plan* plan, int nranks, int heads, int* by_heads, 
  * (every window for a head split): writes min(count, capacity), returns the
  * count. */
 int awa_shard_windows(const awa_plan* plan, int nranks, int heads, int rank, int* windows, int capacity);
+/* The video tokens `rank` computes in a window split, as runs of source-order
+ * tokens: writes min(count, capacity) (first token, tokens) pairs to `runs`,
+ * returns the count (a head split: one run of every token). These are the only
+ * video QKV rows the rank's attention reads (besides the text rows), and the
+ * rows of the output it writes: a caller can copy just these in from the host,
+ * and out. */
+int awa_shard_runs(const awa_plan* plan, int nranks, int heads, int rank, int64_t* runs, int capacity);
 size_t awa_forward_sharded_workspace_bytes(const awa_plan* plan, int nranks, int heads, int head_dim, int out_dtype);
 /* awa_forward over the ranks of `comm`: same arguments and outputs (on every
  * rank: inputs replicated, outputs complete), plus a workspace of

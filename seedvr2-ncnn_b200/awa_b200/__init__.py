@@ -49,7 +49,7 @@ EXPORTED_SYMBOLS = (
     "awa_window_range_video_rows", "awa_partition_windows", "awa_qkv_project", "awa_out_project", "awa_device_status",
     "awa_selftest_bounded_wait", "awa_attention_kernel_kind",
     "awa_comm_unique_id", "awa_comm_create", "awa_comm_wrap", "awa_comm_destroy", "awa_comm_info", "awa_shard_split",
-    "awa_comm_alloc_shared", "awa_comm_free_shared", "awa_shard_windows", "awa_comm_set_push",
+    "awa_comm_alloc_shared", "awa_comm_free_shared", "awa_shard_windows", "awa_comm_set_push", "awa_shard_runs",
     "awa_forward_sharded_workspace_bytes", "awa_forward_sharded",
     "awa_profile_enable", "awa_profile_reset", "awa_profile_collect", "awa_last_error", "awa_version",
     "awa_graph_find_chains", "awa_graph_find_chains_file", "awa_graph_make_dynamic", "awa_manifest_validate",
@@ -156,6 +156,7 @@ def library() -> ctypes.CDLL:
         "awa_comm_info": (i, [p, ctypes.POINTER(i), ctypes.POINTER(i)]),
         "awa_shard_split": (i, [p, i, i, ctypes.POINTER(i), p]),
         "awa_shard_windows": (i, [p, i, i, i, p, i]),
+        "awa_shard_runs": (i, [p, i, i, i, p, i]),
         "awa_forward_sharded_workspace_bytes": (sz, [p, i, i, i, i]),
         "awa_forward_sharded": (i, [p, p, i, i, i, i, p, i64, i64, p, i64, i64, i, p, i64, p, i64, p, sz, p]),
         "awa_attention_kernel_kind": (i, [p, i, i, i, i]),
@@ -471,6 +472,15 @@ class AwaPlan:
         buf = (ctypes.c_int * max(n, 1))()
         lib.awa_shard_windows(self._handle, nranks, heads, rank, ctypes.cast(buf, ctypes.c_void_p), n)
         return list(buf[:n])
+
+    def shard_runs(self, nranks: int, heads: int, rank: int) -> List[Tuple[int, int]]:
+        """The (first token, tokens) runs of video rows `rank` reads and writes."""
+        lib = library()
+        n = lib.awa_shard_runs(self._handle, nranks, heads, rank, None, 0)
+        _check(min(n, 0))
+        buf = (ctypes.c_int64 * max(2 * n, 2))()
+        lib.awa_shard_runs(self._handle, nranks, heads, rank, ctypes.cast(buf, ctypes.c_void_p), n)
+        return [(buf[2 * i], buf[2 * i + 1]) for i in range(n)]
 
     def sharded_workspace_bytes(self, nranks: int, heads: int, head_dim: int, out_dtype) -> int:
         code = out_dtype if isinstance(out_dtype, int) else _dtype_code_of(out_dtype)

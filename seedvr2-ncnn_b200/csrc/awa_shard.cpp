@@ -714,6 +714,26 @@ int awa_shard_windows(const awa_plan* plan, int nranks, int heads, int rank, int
     return (int)mine.size();
 }
 
+int awa_shard_runs(const awa_plan* plan, int nranks, int heads, int rank, int64_t* runs, int capacity)
+{
+    awa_plan_info info;
+    if (!plan || nranks <= 0 || heads <= 0 || rank < 0 || rank >= nranks || capacity < 0 ||
+        (capacity > 0 && !runs) || awa_plan_get_info(plan, &info) != AWA_OK)
+        return fail(AWA_ERR_INVALID, "awa_shard_runs: invalid arguments");
+    const Split s = make_split(plan, info, nranks, heads);
+    std::vector<std::pair<int64_t, int64_t>> mine;
+    if (s.by_heads)
+        mine.emplace_back(0, info.source_tokens);  // every token (a head slice of each row)
+    else
+        mine = band_runs(s, info, s.rank_bands[rank].data(), (int)s.rank_bands[rank].size());
+    for (size_t i = 0; i < mine.size() && (int)i < capacity; i++)
+    {
+        runs[2 * i] = mine[i].first;
+        runs[2 * i + 1] = mine[i].second;
+    }
+    return (int)mine.size();
+}
+
 size_t awa_forward_sharded_workspace_bytes(const awa_plan* plan, int nranks, int heads, int head_dim, int out_dtype)
 {
     awa_plan_info info;

@@ -109,6 +109,14 @@ def _rank_main(rank: int, world: int, port: int, case, result_dir: str):
             partial += attended[cu[w + 1] - text:cu[w + 1]]  # window order, fp32
         if not by_heads:
             assert int(owned[:, 0].sum()) == sum(plan.range_video_rows(w, w + 1) for w in windows)
+        # awa_shard_runs: exactly the video rows these windows read and write
+        runs = plan.shard_runs(world, h, rank)
+        covered = np.zeros(cfg.source_tokens, np.int32)
+        for first, count in runs:
+            assert count > 0
+            covered[first:first + count] += 1
+        assert covered.max(initial=0) <= 1
+        np.testing.assert_array_equal(covered, (owned[:, 0] > 0) if not by_heads else np.ones_like(covered))
         # the exchange: all-reduce of the partials (a head split's are disjoint),
         # all-gather of the video rows
         total = torch.from_numpy(partial)
