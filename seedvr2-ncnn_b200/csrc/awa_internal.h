@@ -90,7 +90,7 @@ struct AttnArgs
     // fused: [window - window_begin][text][H][d] text rows of each window, fp32
     // (SIMT kernel) or bf16 (tcgen05 kernel)
     float* text_partial = nullptr;
-    // work list: (window, q tile) items (SIMT: 64-row tiles; tcgen05: pairs of
+    // work list: (window, q tile) items (SIMT: 128-row tiles; tcgen05: pairs of
     // 128-row tiles), each taken for every head
     const int2* items = nullptr;
     int item_count = 0;
@@ -226,7 +226,7 @@ struct ProfileScope
 };
 
 constexpr int kTcRowsPerTile = 128;   // query rows of one tcgen05 tile (a work item holds two)
-constexpr int kSimtRowsPerTile = 64;  // query rows of one SIMT work item
+constexpr int kSimtRowsPerTile = 128;  // query rows of one SIMT work item
 constexpr int kMaxHeadDim = 128;
 
 }  // namespace awa

@@ -37,7 +37,7 @@ struct awa_plan
     std::vector<short4> position_coords;
     std::vector<int2> items_tc;         // fused tcgen05 path: (window, pair of 128-row q tiles), longest first
     std::vector<int2> items_tc_packed;  // packed tcgen05 path: same, over the packed rows
-    std::vector<int2> items_simt;       // (window, 64-row q tile)
+    std::vector<int2> items_simt;       // (window, 128-row q tile)
     std::vector<double> window_cost;    // L^2 per window
     bool tc_slabs = false;              // every window is a clipped piece of a nominal-size window
     // device copies
