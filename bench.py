@@ -368,13 +368,9 @@ def run_sharded(args, rank, world, local_rank):
     # the QKV rows its windows read (its bands' token runs, awa_shard_runs, and
     # the text rows), runs the sharded layer, and copies its runs of the video
     # output back; rank 0 also copies the text output. Together the ranks move
-    # the whole input in and the whole output out every step. Steps alternate
-    # over two sets of device buffers, as a stream of layers would run: the copy
-    # in of step i + 1 (one stream) and the copy out of step i - 1 (another)
-    # overlap the layer of step i (the host link is full duplex).
+    # the whole input in and the whole output out every step.
     e2e_ms, e2e_steps = None, 0
     in_bytes = out_bytes = 0
-    extra_out = []
     if not args.no_e2e:
         e2e_steps = max(3, min(args.steps, args.e2e_steps))
         runs = plan.shard_runs(world, HEADS, rank)
@@ -394,59 +390,31 @@ def run_sharded(args, rank, world, local_rank):
         host_t = torch.empty(text_qkv.shape, dtype=dtype, pin_memory=True)
         host_t.copy_(text_qkv)
         host_ot = torch.empty(text_out.shape, dtype=dtype, pin_memory=True)
-        if direct:
-            extra_out.append(comm.shared_tensor((n_v, HEADS, HEAD_DIM), dtype))
-        else:
-            extra_out.append(torch.empty_like(video_out))
-        bufs = [(torch.zeros_like(video_qkv), torch.empty_like(text_qkv), vo, torch.empty_like(text_out))
-                for vo in (video_out, extra_out[0])]
-        s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
-        in_done = [torch.cuda.Event() for _ in range(2)]
-        fwd_done = [torch.cuda.Event() for _ in range(2)]
-        out_done = [torch.cuda.Event() for _ in range(2)]
+        dev_v = torch.zeros_like(video_qkv)
+        dev_t = torch.empty_like(text_qkv)
 
-        def e2e_step(i):
-            b = i % 2
-            dv, dt, vo, to = bufs[b]
-            with torch.cuda.stream(s_in):
-                if i >= 2:
-                    s_in.wait_event(fwd_done[b])  # the layer of step i - 2 has read these inputs
-                at = 0
-                for first, count in runs:
-                    dv[first:first + count].copy_(host_v[at:at + count], non_blocking=True)
-                    at += count
-                dt.copy_(host_t, non_blocking=True)
-                in_done[b].record(s_in)
-            stream.wait_event(in_done[b])
-            if i >= 2:
-                stream.wait_event(out_done[b])  # step i - 2's outputs are copied out
-            plan.forward_sharded(comm, dv, dt, prec, out_dtype=dtype, workspace=workspace, video_out=vo,
-                                 text_out=to, stream=stream)
-            fwd_done[b].record(stream)
-            with torch.cuda.stream(s_out):
-                s_out.wait_event(fwd_done[b])
-                at = 0
-                for first, count in runs:
-                    host_o[at:at + count].copy_(vo[first:first + count], non_blocking=True)
-                    at += count
-                if rank == 0:
-                    host_ot.copy_(to, non_blocking=True)
-                out_done[b].record(s_out)
+        def e2e_step():
+            at = 0
+            for first, count in runs:
+                dev_v[first:first + count].copy_(host_v[at:at + count], non_blocking=True)
+                at += count
+            dev_t.copy_(host_t, non_blocking=True)
+            step(dev_v, dev_t)
+            at = 0
+            for first, count in runs:
+                host_o[at:at + count].copy_(video_out[first:first + count], non_blocking=True)
+                at += count
+            if rank == 0:
+                host_ot.copy_(text_out, non_blocking=True)
 
-        for i in range(2):
-            e2e_step(i)
+        for _ in range(2):
+            e2e_step()
         torch.cuda.synchronize()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        s_in.wait_event(e0)
-        s_out.wait_event(e0)
-        for i in range(e2e_steps):
-            e2e_step(i)
-        for st in (s_in, s_out):
-            done = torch.cuda.Event()
-            done.record(st)
-            stream.wait_event(done)
+        for _ in range(e2e_steps):
+            e2e_step()
         e1.record(stream)
         torch.cuda.synchronize()
         barrier()
@@ -456,8 +424,7 @@ def run_sharded(args, rank, world, local_rank):
     clock = clocks.stop()
     awa_b200.device_status()
     if direct:
-        for t_ in [video_out] + extra_out:
-            comm.free_shared(t_)
+        comm.free_shared(video_out)
     comm.destroy()
 
     hbm_peak, tensor_peak, peak_src = measured_peaks()
@@ -491,8 +458,7 @@ def run_sharded(args, rank, world, local_rank):
                 "value": round(W / (e2e_ms / 1000.0), 2), "unit": UNIT, "h2d_bytes_per_step": in_bytes,
                 "d2h_bytes_per_step": out_bytes, "steps": e2e_steps, "ms_per_step": round(e2e_ms, 4),
                 "how": "each rank copies in the QKV rows of its windows (its token runs + the text rows) and "
-                       "copies out its runs of the video output, rank 0 the text output; steps alternate over "
-                       "two buffer sets so copies in and out overlap the layer"},
+                       "copies out its runs of the video output; rank 0 the text output"},
             "roofline": {"bound": "hbm", "kernel": attn_name, "achieved": round(achieved, 1), "peak": hbm_peak,
                          "unit": "GB/s", "frac": round(achieved / hbm_peak, 4), "traffic": None,
                          "peak_source": peak_src, "algorithmic_bytes": alg_bytes, "kernel_ms": round(attn_ms, 5),
