@@ -1,6 +1,7 @@
 """One AWA layer split over 2 GPUs with NCCL (awa_forward_sharded).
 
-Two processes, one per GPU (tests/sharded_worker.py), run each layer sharded
+Two processes (AWA_TEST_WORLD of them, up to the GPUs present, when that
+variable is set), one per GPU (tests/sharded_worker.py), run each layer sharded
 and on their own GPU alone. Windows are independent, so the video rows a rank
 receives through the all-gather must equal, bit for bit, the single-GPU
 awa_forward's; the text mean sums the same per-window values in another
@@ -10,8 +11,8 @@ Covered: the window split (cfg2, cfg2 shifted, cfg4, cfg5-fp32 shifted) and
 the head split of a layer with fewer than 4 windows per rank (cfg1, 4 windows),
 bf16 (tensor cores) and fp32 (SIMT), fp32 and block-dtype outputs, and the
 direct mode, where the video output lies in a buffer shared over the ranks
-(awa_comm_alloc_shared) and the tensor-core kernel stores each row into every
-rank's copy over NVLink.
+(awa_comm_alloc_shared) and each rank's rows are pushed into every rank's copy
+over NVLink, by the copy engines and by the SM push kernel.
 """
 
 import json
@@ -30,7 +31,9 @@ if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
     pytest.skip("needs 2 CUDA devices", allow_module_level=True)
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-WORLD = 2
+WORLD = int(os.environ.get("AWA_TEST_WORLD", "2"))
+if WORLD < 2 or torch.cuda.device_count() < WORLD:
+    pytest.skip(f"needs {WORLD} CUDA devices", allow_module_level=True)
 
 
 @pytest.fixture(scope="module")
@@ -61,11 +64,12 @@ def test_sharded_layer_matches_single_gpu(rank_results, name):
     for rank, res in enumerate(rank_results):
         r = res[name]
         assert r["status"] == 0, (rank, r)
-        assert r["by_heads"] == ("heads" in name), r
+        if WORLD == 2:
+            assert r["by_heads"] == ("heads" in name), r
         assert r["video_equal"], (rank, name)
         assert r["text_rel"] < 1e-6, (rank, r["text_rel"])
-        # the video output in a buffer shared over the ranks (P2P stores from the
-        # tensor-core kernel; the fp32 layers take the all-gather path)
+        # the video output in a buffer shared over the ranks, rows pushed by the
+        # copy engines and by the SM push kernel
         assert r["direct_video_equal"], (rank, name, "direct")
         assert r["direct_text_rel"] < 1e-6, (rank, r["direct_text_rel"])
         block_tol = 1e-2 if bf16 else 1e-6
