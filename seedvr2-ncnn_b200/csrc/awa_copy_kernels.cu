@@ -645,39 +645,20 @@ int launch_text_scale(int rows, int heads, int head_dim, const float* text_sum, 
 
 // Byte runs of this GPU's buffer pushed into the same offsets of peer
 // buffers over NVLink (plain 16-byte loads here, 16-byte stores there):
-// blockIdx.y picks the run, the threads stride through it, each loading
-// kPushUnroll units before it stores them, so that a grid of one block per SM
-// still keeps enough loads in flight. kPushThreads threads of at most 64
-// registers: one block fits on an SM beside the attention kernel's. Every
-// thread fences at system scope before it ends, so the collective the host
-// enqueues next orders the stores before the peers' reads.
-constexpr int kPushThreads = 128;
-constexpr int kPushUnroll = 4;
-
-__global__ void __launch_bounds__(kPushThreads, 8) push_runs_kernel(const uint4* __restrict__ local, PushPeers peers,
-                                                                    PushRuns runs)
+// blockIdx.y picks the run, the threads stride through it. Every thread
+// fences at system scope before it ends, so the collective the host enqueues
+// next orders the stores before the peers' reads.
+__global__ void __launch_bounds__(256) push_runs_kernel(const uint4* __restrict__ local, PushPeers peers,
+                                                        PushRuns runs)
 {
     const int r = blockIdx.y;
     const int64_t first = runs.first[r], count = runs.count[r];
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += kPushUnroll * stride)
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
     {
-        uint4 v[kPushUnroll];
-#pragma unroll
-        for (int u = 0; u < kPushUnroll; u++)
-            if (i + u * stride < count)
-                v[u] = __ldg(local + first + i + u * stride);
-#pragma unroll
-        for (int q = 0; q < kMaxPushPeers; q++)  // constant indices: the peer table stays in parameter space
-        {
-            if (q >= peers.count)
-                break;
-            uint4* dst = peers.ptr[q] + first + i;
-#pragma unroll
-            for (int u = 0; u < kPushUnroll; u++)
-                if (i + u * stride < count)
-                    dst[u * stride] = v[u];
-        }
+        const uint4 v = __ldg(local + first + i);
+#pragma unroll 1
+        for (int q = 0; q < peers.count; q++)
+            peers.ptr[q][first + i] = v;
     }
     __threadfence_system();
 }
@@ -699,8 +680,7 @@ int launch_rows_to_bf16(const void* src, int64_t ts, int64_t qs, int tokens, int
     return (int)cudaGetLastError();
 }
 
-int launch_push_runs(const void* local, const PushPeers& peers, const PushRuns& runs, cudaStream_t stream,
-                     int max_blocks)
+int launch_push_runs(const void* local, const PushPeers& peers, const PushRuns& runs, cudaStream_t stream)
 {
     if (runs.n <= 0 || peers.count <= 0)
         return 0;
@@ -709,18 +689,9 @@ int launch_push_runs(const void* local, const PushPeers& peers, const PushRuns& 
     int64_t most = 0;
     for (int r = 0; r < runs.n; r++)
         most = std::max<int64_t>(most, runs.count[r]);
-    // the SMs keep the shared-memory-heavy configuration the attention kernel
-    // needs, so its next launch can place a block beside a push block
-    static const cudaError_t carveout = cudaFuncSetAttribute(
-        push_runs_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
-    if (carveout != cudaSuccess)
-        return (int)carveout;
     ProfileScope prof("awa_push_runs", stream);
-    const int64_t budget = max_blocks > 0 ? max_blocks : 2368;  // blocks of the whole launch
-    const int64_t per_block = (int64_t)kPushUnroll * kPushThreads;
-    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((most + per_block - 1) / per_block, budget / runs.n));
-    push_runs_kernel<<<dim3(blocks, runs.n), kPushThreads, 0, stream>>>(static_cast<const uint4*>(local), peers,
-                                                                         runs);
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((most + 255) / 256, 1184 / runs.n + 1));
+    push_runs_kernel<<<dim3(blocks, runs.n), 256, 0, stream>>>(static_cast<const uint4*>(local), peers, runs);
     return (int)cudaGetLastError();
 }
 

@@ -143,9 +143,7 @@ struct PushRuns
 };
 // Copies the runs of `local` into every peer at the same offsets (SM loads
 // and NVLink stores), with a system-scope fence at the end of every thread.
-// max_blocks > 0 caps the blocks of the launch (at least one per run).
-int launch_push_runs(const void* local, const PushPeers& peers, const PushRuns& runs, cudaStream_t stream,
-                     int max_blocks = 0);
+int launch_push_runs(const void* local, const PushPeers& peers, const PushRuns& runs, cudaStream_t stream);
 int launch_shard_copy(const PlanDevice& plan, int heads, int head_dim, int window_begin, int window_end, int dtype,
                       const void* src, int64_t src_stride, void* dst, int64_t dst_stride, int to_source,
                       cudaStream_t stream);

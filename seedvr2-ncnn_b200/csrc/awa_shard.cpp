@@ -369,25 +369,22 @@ int push_streams(awa_comm* c)
 }
 
 // The rank's bands cut into at most kPushChunks runs: returns the band-list
-// offsets of the cuts (first 0, last the band count). The chunk costs change
-// geometrically: halving when the copies are faster than the attention (copy
-// engines with one peer: only the last chunk's copies are not hidden behind a
-// later chunk's attention), doubling when the copies are the slower part (the
-// push kernel with several peers: the pushes start as early as they can and
-// then never wait for the attention).
-std::vector<int> push_chunks(const Split& s, int rank, bool growing)
+// offsets of the cuts (first 0, last the band count). The chunk costs shrink
+// geometrically (halving), since only the last chunk's copies are not hidden
+// behind a later chunk's attention.
+std::vector<int> push_chunks(const Split& s, int rank)
 {
     const auto& rb = s.rank_bands[rank];
     double total = 0;
     for (int b : rb)
         total += s.bands[b].cost;
     const int chunks = std::max(1, std::min<int>(kPushChunks, (int)rb.size()));
-    // shares 2^(chunks-1) : ... : 2 : 1 of the cost (or 1 : 2 : ... growing), cumulative targets
+    // shares 2^(chunks-1) : ... : 2 : 1 of the cost, cumulative targets
     std::vector<double> target;
     double sum = 0, unit = total / ((1 << chunks) - 1);
     for (int c = 0; c < chunks - 1; c++)
     {
-        sum += unit * (1 << (growing ? c : chunks - 1 - c));
+        sum += unit * (1 << (chunks - 1 - c));
         target.push_back(sum);
     }
     std::vector<int> cuts{0};
@@ -440,11 +437,9 @@ int join_pushes(awa_comm* c, cudaStream_t st)
 }
 
 // Pushes token runs into every peer with the SM copy kernel on `st` (after the
-// work enqueued there), in launches of at most kMaxPushRuns runs; max_blocks >
-// 0 caps the blocks of each launch.
+// work enqueued there), in launches of at most kMaxPushRuns runs.
 int push_runs_kernel(const std::vector<std::pair<int64_t, int64_t>>& runs, unsigned char* local,
-                     const std::vector<unsigned char*>& peers, int64_t token_bytes, int64_t row_bytes, cudaStream_t st,
-                     int max_blocks = 0)
+                     const std::vector<unsigned char*>& peers, int64_t token_bytes, int64_t row_bytes, cudaStream_t st)
 {
     awa::PushPeers pp{};
     pp.count = (int)peers.size();
@@ -459,7 +454,7 @@ int push_runs_kernel(const std::vector<std::pair<int64_t, int64_t>>& runs, unsig
             pr.first[pr.n] = runs[i].first * token_bytes / 16;
             pr.count[pr.n] = ((runs[i].second - 1) * token_bytes + row_bytes) / 16;
         }
-        const int e = awa::launch_push_runs(local, pp, pr, st, max_blocks);
+        const int e = awa::launch_push_runs(local, pp, pr, st);
         if (e)
             return cuda_status(static_cast<cudaError_t>(e), "peer push kernel");
     }
@@ -889,41 +884,19 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
                               (comm->push_mode == AWA_PUSH_AUTO && (int)peers.size() >= 3));
     if (direct && push_kernel)
     {
-        // chunk by chunk, growing: attention of the chunk's windows, then the SM
-        // copy kernel pushes its rows into every peer (NVLink stores) on a side
-        // stream, one block per SM beside the next chunk's attention; the last
-        // chunk's push takes the whole GPU
-        const std::vector<int> cuts = push_chunks(s, r, true);
+        // one attention launch over the rank's windows, then the SM copy kernel
+        // pushes its rows into every peer (NVLink stores from all SMs)
         const auto& rb = s.rank_bands[r];
-        const size_t psz = awa_attention_kernel_kind(plan, precision, in_dtype, heads, head_dim) == 1 ? 2 : 4;
-        cudaStream_t ps = comm->push_stream[0];
-        int sms = 0;
-        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, comm->device) != cudaSuccess || sms <= 0)
-            sms = 148;
-        size_t done = 0;  // windows (partial slots) of the chunks so far
-        for (size_t c = 0; c + 1 < cuts.size() && rc == AWA_OK; c++)
-        {
-            const std::vector<int> set = band_windows(s, rb.data() + cuts[c], cuts[c + 1] - cuts[c]);
-            const size_t off = done * window_partial * psz;
-            rc = awa::attention_set(plan, precision, heads, head_dim, set.data(), (int)set.size(), in_dtype,
-                                    video_qkv, video_token_stride, video_qkv_stride, text_qkv, text_token_stride,
-                                    text_qkv_stride, out_dtype, video_out, video_token_stride_out, partials + off,
-                                    partial_bytes - off, &partial_dtype, st);
-            done += set.size();
-            const bool last = c + 2 == cuts.size();
-            if (rc == AWA_OK)
-                rc = cuda_status(cudaEventRecord(comm->chunk_ready[c], st), "push chunk event");
-            if (rc == AWA_OK)
-                rc = cuda_status(cudaStreamWaitEvent(ps, comm->chunk_ready[c], 0), "push chunk wait");
-            if (rc == AWA_OK)
-                rc = push_runs_kernel(band_runs(s, info, rb.data() + cuts[c], cuts[c + 1] - cuts[c]),
-                                      static_cast<unsigned char*>(video_out), peers, tbytes, rbytes, ps,
-                                      last ? 0 : sms);
-        }
+        rc = awa::attention_set(plan, precision, heads, head_dim, mine.data(), (int)mine.size(), in_dtype, video_qkv,
+                                video_token_stride, video_qkv_stride, text_qkv, text_token_stride, text_qkv_stride,
+                                out_dtype, video_out, video_token_stride_out, partials, partial_bytes, &partial_dtype,
+                                st);
         if (rc == AWA_OK)
-            rc = awa::text_partial_sum(plan, heads, head_dim, partial_dtype, partials, 0, (int)done, text_sum, st);
+            rc = push_runs_kernel(band_runs(s, info, rb.data(), (int)rb.size()), static_cast<unsigned char*>(video_out),
+                                  peers, tbytes, rbytes, st);
         if (rc == AWA_OK)
-            rc = join_pushes(comm, st);
+            rc = awa::text_partial_sum(plan, heads, head_dim, partial_dtype, partials, 0, (int)mine.size(), text_sum,
+                                       st);
         if (rc == AWA_OK)
             rc = nccl_status(n, n->all_reduce(text_sum, text_sum, (size_t)info.text_tokens * row, ncclFloat32, ncclSum,
                                               comm->comm, st),
@@ -936,7 +909,7 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
     {
         // chunk by chunk: attention of the chunk's windows, then its rows to the
         // peers on the copy engines while the next chunk computes
-        const std::vector<int> cuts = push_chunks(s, r, false);
+        const std::vector<int> cuts = push_chunks(s, r);
         const auto& rb = s.rank_bands[r];
         const size_t psz = awa_attention_kernel_kind(plan, precision, in_dtype, heads, head_dim) == 1 ? 2 : 4;
         size_t done = 0;  // windows (partial slots) of the chunks so far
