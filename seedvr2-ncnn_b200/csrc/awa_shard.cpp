@@ -774,14 +774,16 @@ int awa_forward_sharded(const awa_plan* plan, awa_comm* comm, int precision, int
     const int64_t row = (int64_t)heads * head_dim;
     int rc = AWA_OK;
 
-    // Direct mode: video_out lies in a buffer shared over the ranks. The copy
-    // engines then push this rank's video rows into every other rank's copy of
-    // video_out over NVLink (peer copies on a side stream), chunk by chunk as
-    // the attention kernel finishes them, so the transfer overlaps the next
-    // chunk's attention and needs no all-gather, staging or scatter. An entry
-    // barrier keeps any rank from writing before every rank is done with the
-    // previous contents; the text collective at the end, enqueued after the
-    // copies, orders them before every rank's later reads.
+    // Direct mode: video_out lies in a buffer shared over the ranks. This
+    // rank's video rows then go straight into every other rank's copy of
+    // video_out over NVLink, with no all-gather, staging or scatter: with one
+    // peer the copy engines push them chunk by chunk as the attention kernel
+    // finishes them (peer copies on side streams, overlapping the next chunk's
+    // attention); with more peers (or when asked) the SM push kernel pushes
+    // them after the attention. An entry barrier keeps any rank from writing
+    // before every rank is done with the previous contents; the text
+    // collective at the end, enqueued after the pushes, orders them before
+    // every rank's later reads.
     const size_t video_span = (size_t)(info.source_tokens - 1) * video_token_stride_out * osz + (size_t)row * osz;
     const SharedBuffer* shared = find_shared(comm, video_out, video_span);
     const bool direct = shared != nullptr && R > 1;
